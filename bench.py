@@ -1,0 +1,406 @@
+"""Benchmark of the B200 VD-TTFS engine (one JSON line on rank 0).
+
+Default workload: BASELINE config 3, the VGG-16 TTFS-SNN at batch 256 per GPU
+(T=80, delta=8, TIME_FIRE_START=40), weak scaling over the GPUs of one box.
+A step = one batch through the whole network (encode, 15 x {bucketize,
+integrate}, 5 pools, membrane readout, argmax) + the NCCL all-gather of the
+int32 predictions when N > 1.
+
+  value   images/s over all ranks, input pixels already in HBM, device-timed
+          with CUDA events per step (max over ranks); a 256 MiB L2-flush write
+          runs between steps, outside the timed events.
+  e2e     the same through vdt_infer_host: pinned host pixels -> H2D -> the
+          network -> D2H of the logits and predictions, every step.
+  roofline  the integrator (k_integrate, all launches of a step) timed live
+          with CUDA events around each launch (eager profiling pass), against
+          its algorithmic bytes: events read (8 B each), chunk offsets read,
+          first-spike map written, weights read once per launch.
+  cpu_baseline  the CPU oracle port (OpenMP over all host cores) on a bounded
+          sample of the same workload.
+
+`--impl reference` times the reference algorithm's CPU implementation (the
+oracle port; the reference ships no CPU implementation of this path) and
+prints its own line; under torchrun only rank 0 works.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vd-ttfs_b200"))
+
+CONFIGS = {
+    # name: (net factory, config id, batch per GPU, zero fraction, scaling)
+    "vgg16": ("vgg16", 3, 256, 0.0, "weak"),
+    "lenet5": ("lenet5", 2, 65536, 0.8, "strong"),
+    "lenet5_b1024": ("lenet5", 1, 1024, 0.8, "weak"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    ap.add_argument("--config", default="vgg16", choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- clocks --
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index, enabled=True):
+        self.gpu = gpu_index
+        self.proc = None
+        self.enabled = enabled
+        self.lines = []
+
+    def start(self):
+        if not self.enabled:
+            return
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(mx)),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------- peaks --
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------- algorithmic --
+def integrator_bytes(net, events_per_layer, B):
+    """Algorithmic bytes of every k_integrate launch of one step (and of the
+    membrane readout on the last layer): 8 B per event read (cin + t_in),
+    4 B per chunk offset read, 4 B per output neuron written, the layer's
+    weights read once."""
+    OS = net.n_chunks + 1
+    total = 0
+    for (l, shp, E) in zip(net.layers, net.shapes(), events_per_layer):
+        H_in, W_in, C_in, H_out, W_out, C_out = shp
+        n_out = B * H_out * W_out * C_out
+        wts = (l.k * l.k if l.kind == 0 else 1) * C_in * C_out
+        if l.out == 1:       # membrane readout reads the dense input map
+            total += 4 * B * C_in + 4 * n_out + 4 * wts
+            continue
+        cols = B if l.kind == 1 else B * H_in * W_in
+        total += 8 * E + 4 * cols * OS + 4 * n_out + 4 * wts
+    return total
+
+
+def launches_per_step(net, pixels=True):
+    n = 1 if pixels else 0
+    for l in net.layers:
+        n += 1 if l.out == 1 else 2
+        n += 1 if l.pool_after else 0
+    return n + 1        # readout
+
+
+# --------------------------------------------------------------- engine run --
+def run_engine(a):
+    import torch
+    import torch.distributed as dist
+    from vdttfs import engine as E, nets, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    netname, cfg_id, Bcfg, zf, scaling = CONFIGS[a.config]
+    net = nets.NETS[netname]()
+    B = Bcfg // world if scaling == "strong" else Bcfg
+    layers = synth.kaiming_layers(net, cfg_id)
+    img = synth.images(cfg_id, B, net.in_h, net.in_w, net.in_c, zf, stream=rank)
+    model = E.Model(net, layers, device=local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx = E.Context(model, B, stream=stream.cuda_stream)
+
+    x_dev = torch.from_numpy(img).to(dev)
+    out = torch.empty((B, net.n_classes), dtype=torch.float32, device=dev)
+    pred = torch.empty((B,), dtype=torch.int32, device=dev)
+    gathered = torch.empty((world * B,), dtype=torch.int32, device=dev) if world > 1 else None
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        ctx.infer(x_dev, pixels=True, out=out, pred=pred)
+        if world > 1:
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(gathered, pred)
+
+    # ---- counters (events / fetched synapses) on one untimed batch
+    ctx.set_counting(True)
+    with torch.cuda.stream(stream):
+        ctx.infer(x_dev, pixels=True, out=out, pred=pred)
+    stream.synchronize()
+    ev_total, fetched = ctx.counters()
+    ctx.set_counting(False)
+
+    # ---- timed device steps
+    for _ in range(a.warmup):
+        with torch.cuda.stream(stream):
+            step()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local, enabled=(rank == 0 and not a.no_clocks))
+    clocks.start()
+    times = []
+    for _ in range(a.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(1)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        stream.synchronize()
+        times.append(e0.elapsed_time(e1))
+    clk = clocks.stop()
+    tot_ms = float(np.sum(times))
+    if world > 1:
+        t = torch.tensor([tot_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tot_ms = float(t.item())
+    value = world * B * a.steps / (tot_ms / 1e3)
+
+    # ---- end to end through host buffers (pinned), every step
+    h_in = torch.from_numpy(img).pin_memory()
+    h_out = torch.empty((B, net.n_classes), dtype=torch.float32).pin_memory()
+    h_pred = torch.empty((B,), dtype=torch.int32).pin_memory()
+    for _ in range(max(1, a.warmup)):
+        ctx.infer_host(h_in, pixels=True, out=h_out, pred=h_pred)
+    if world > 1:
+        dist.barrier()
+    e_times = []
+    for _ in range(a.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(1)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        ctx.infer_host(h_in, pixels=True, out=h_out, pred=h_pred)
+        with torch.cuda.stream(stream):
+            e1.record(stream)
+        stream.synchronize()
+        e_times.append(e0.elapsed_time(e1))
+    e_ms = float(np.sum(e_times))
+    if world > 1:
+        t = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e = world * B * a.steps / (e_ms / 1e3)
+
+    # ---- integrator roofline: per-launch CUDA events (eager profiling pass)
+    ctx.set_profiling(True)
+    ctx.layer_times()
+    prof_steps = max(3, min(a.steps, 10))
+    for _ in range(prof_steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(1)
+            ctx.infer(x_dev, pixels=True, out=out, pred=pred)
+    bkt_ms, int_ms, pool_ms, nb = ctx.layer_times()
+    ctx.set_profiling(False)
+    # events per layer from the oracle-independent bucket counts: re-run with counting per layer
+    per_layer_events = layer_events(E, net, layers, x_dev, B, dev)
+    int_bytes = integrator_bytes(net, per_layer_events, B)
+    int_step_ms = float(np.sum(int_ms)) / nb
+    peak, peak_kind = peaks()
+    achieved = int_bytes / (int_step_ms / 1e3) / 1e9
+
+    if world > 1:
+        dist.barrier()
+    res = None
+    if rank == 0:
+        res = {
+            "metric": "images_per_sec", "value": round(value, 1), "unit": "images/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(tot_ms / a.steps, 4), "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded uniform pixels, Kaiming weights, see vdttfs/synth.py)",
+            "config": {"workload": f"{netname} C{cfg_id}", "model": netname, "global_batch": world * B,
+                       "batch_per_gpu": B, "T": net.T, "delta": net.delta, "fire_start": net.tfs,
+                       "zero_frac": zf, "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) between steps"},
+            "e2e": {"value": round(e2e, 1), "unit": "images/s",
+                    "h2d_bytes_per_step": int(img.nbytes),
+                    "d2h_bytes_per_step": int(B * net.n_classes * 4 + B * 4)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "kernel": "k_integrate (all launches of a step)",
+                         "peak_source": peak_kind,
+                         "algorithmic_bytes_per_step": int(int_bytes),
+                         "integrate_ms_per_step": round(int_step_ms, 4),
+                         "bucketize_ms_per_step": round(float(np.sum(bkt_ms)) / nb, 4),
+                         "pool_ms_per_step": round(float(np.sum(pool_ms)) / nb, 4)},
+            "gpu_launches": launches_per_step(net) * a.steps,
+            "events_per_image": round(ev_total / B, 1),
+            "fetched_synapses_per_image": round(fetched / B, 1),
+            "clocks": clk,
+        }
+        if not a.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline(net, layers, img, cfg_id, budget_s=20.0)
+    if world > 1:
+        del ctx
+        dist.destroy_process_group()
+    return res
+
+
+def layer_events(E, net, layers, x_dev, B, dev):
+    """Per-layer kept-event counts (exact), from the engine's own counters."""
+    from vdttfs import nets
+    import torch
+    per = []
+    # run the network layer by layer through the per-stage API
+    maps = None
+    ctx = E.Context(E.Model(net, layers), B)
+    maps, _, _ = ctx.trace(x_dev, pixels=True)
+    cfg = E.time_cfg(net)
+    enc = E.encode_image(x_dev.reshape(-1), net.encoder, net.tc_in, net.td_in, net.T).reshape(x_dev.shape)
+    x = enc
+    for li, (l, shp) in enumerate(zip(net.layers, net.shapes())):
+        H_in, W_in, C_in, H_out, W_out, C_out = shp
+        if l.out == nets.OUT_VMEM:
+            per.append(0)
+        else:
+            n_cols = B if l.kind == nets.KIND_FC else B * H_in * W_in
+            off, _, _ = E.bucketize(x.reshape(-1), n_cols, C_in, cfg)
+            per.append(int(off[:, -1].sum().item()))
+        y = maps[li]
+        if l.pool_after:
+            y = E.pooling(y.reshape(-1), B, H_out, W_out, C_out)
+        x = y
+    torch.cuda.synchronize()
+    ctx.close()
+    return per
+
+
+# --------------------------------------------------------------- CPU legs --
+def cpu_baseline(net, layers, img, cfg_id, budget_s=20.0):
+    """Oracle port on a bounded sample: grow the sample until one pass takes
+    ~budget_s / 4, then time passes until ~budget_s elapsed."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cores = os.cpu_count() or 1
+    n = 2
+    while True:
+        x = O.encode_linear(img[:n], net.T)
+        t0 = time.perf_counter()
+        O.run_net(net, layers, x)
+        dt = time.perf_counter() - t0
+        if dt > budget_s / 4 or n >= img.shape[0]:
+            break
+        n = min(img.shape[0], n * 2)
+    reps, t_tot = 0, 0.0
+    while t_tot < budget_s * 0.75 and reps < 8:
+        x = O.encode_linear(img[:n], net.T)
+        t0 = time.perf_counter()
+        O.run_net(net, layers, x)
+        t_tot += time.perf_counter() - t0
+        reps += 1
+    return {"value": round(n * reps / t_tot, 2), "unit": "images/s", "cores": cores, "kind": "port",
+            "sample": f"{reps} passes of {n} images of the same workload (linear encode + network), "
+                      f"OpenMP over {cores} threads"}
+
+
+def run_reference(a):
+    from vdttfs import nets, synth
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    netname, cfg_id, Bcfg, zf, scaling = CONFIGS[a.config]
+    net = nets.NETS[netname]()
+    layers = synth.kaiming_layers(net, cfg_id)
+    cores = os.cpu_count() or 1
+    n = 8 if netname == "vgg16" else 512
+    img = synth.images(cfg_id, n, net.in_h, net.in_w, net.in_c, zf, stream=0)
+    for _ in range(a.warmup):
+        O.run_net(net, layers, O.encode_linear(img, net.T))
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        O.run_net(net, layers, O.encode_linear(img, net.T))
+    dt = time.perf_counter() - t0
+    v = round(n * a.steps / dt, 2)
+    return {"impl": "reference", "metric": "images_per_sec", "value": v, "unit": "images/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(dt / a.steps * 1e3, 3), "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": f"{netname} C{cfg_id}", "model": netname, "batch_per_step": n,
+                       "T": net.T, "delta": net.delta},
+            "cpu_baseline": {"value": v, "unit": "images/s", "cores": cores, "kind": "port",
+                             "sample": f"{n} images per step, the CPU port of the reference's "
+                                       f"vdttfs algorithm (oracle/vdt_oracle.c), OpenMP {cores} threads"},
+            "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    a = parse()
+    if a.warmup < 3:
+        a.warmup = 3
+    res = run_reference(a) if a.impl == "reference" else run_engine(a)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+/*
+ * vdttfs.h -- C ABI of the B200-native VD-TTFS engine (libvdttfs.so).
+ *
+ * Drop-in for the `vdttfs_cuda` path of Xarlley/VD-TTFS.  The reference has no
+ * library: each task is one .cu program whose `main` hard-codes the network,
+ * and whose per-stage kernels/host helpers are what this header replaces.
+ * File references below are paths inside the reference project:
+ *   t1 = task1_lenet_mnist/vdttfs_cuda/snn_timesorted_earlyexit.cu
+ *   t2 = task2_vgg16_cifar10/vdttfs_cuda/bench_vgg_eventdriven_timesorted_earlyexit.cu
+ *   t3 = task3_dvsgesture/vdttfs_cuda/snn_inference_timesorted.cu
+ *
+ * Conventions
+ *   - Every call returns an int status (VDT_OK = 0); the library never exits
+ *     the process.  vdt_strerror() names a status; vdt_last_error() returns a
+ *     per-thread message with details of the last failure.
+ *   - "d_" pointers are device memory owned by the caller; "h_" pointers are
+ *     host memory.  Calls taking a stream are asynchronous on it (NULL = the
+ *     legacy default stream); the vdt_*_host calls are synchronous.
+ *   - A vdt_model is immutable after load and may be shared by threads; a
+ *     vdt_ctx (workspace + captured CUDA graphs) belongs to one thread/stream.
+ *   - Spike times are fp32; inf_time (9999 in the reference) means "no spike".
+ *   - Compile-time macros of the reference (TIME_WINDOW, CHUNK,
+ *     TIME_FIRE_START, VTH_INIT, INF_TIME) are runtime fields of vdt_time_cfg.
+ */
+#ifndef VDTTFS_H
+#define VDTTFS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct vdt_model vdt_model;
+typedef struct vdt_ctx vdt_ctx;
+typedef void* vdt_stream; /* cudaStream_t */
+
+enum vdt_status {
+    VDT_OK = 0,
+    VDT_ERR_INVALID = 1,     /* bad argument / shape / descriptor */
+    VDT_ERR_BLOB = 2,        /* malformed or truncated weight blob */
+    VDT_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+    VDT_ERR_OOM = 4,         /* device allocation failed */
+    VDT_ERR_UNSUPPORTED = 5, /* valid request outside what the kernels implement */
+    VDT_ERR_CAPACITY = 6     /* batch above the ctx's max_batch */
+};
+
+/* layer kinds / padding / output kind (topology lives in each reference main) */
+enum { VDT_CONV = 0, VDT_FC = 1 };
+enum { VDT_PAD_VALID = 0, VDT_PAD_SAME = 1 };  /* t1 valid conv; t2 pad = K/2 */
+enum { VDT_OUT_FIRE = 0, VDT_OUT_VMEM = 1 };   /* k_conv_bucketed / k_layer_vmem */
+/* LUT_decay index: tb (t1:128,144) or clamp((int)t_in, 0, T) (t2:132,150) */
+enum { VDT_LUT_BY_TB = 0, VDT_LUT_BY_TIN = 1 };
+/* where the tables come from: a device kernel (exp in double, rounded) or
+   the host libm expf exactly like update_LUTs (bit-identical tables) */
+enum { VDT_LUT_DEVICE = 0, VDT_LUT_HOST_LIBM = 1 };
+/* readouts: t1:313-315 argmin (-1 if nothing fires), t3:295-296 argmin with
+   class 0 as the start, t2:391-392 argmax of the membrane */
+enum { VDT_READ_ARGMIN_FIRST = 0, VDT_READ_ARGMIN_LOWEST = 1, VDT_READ_ARGMAX = 2 };
+/* input encoders: none (spike times given), k_encode_image's log encoder
+   (t1:32-42, t2:32-42), or the linear t = floor((1 - x) * T) */
+enum { VDT_ENC_NONE = 0, VDT_ENC_LOG = 1, VDT_ENC_LINEAR = 2 };
+/* bucket index: tb = max(0, floor(t - fire_start)) (t1:58, t2:59) or
+   tb = (int)t with 0 <= tb < T (t3:79,99) */
+enum { VDT_TB_FLOOR_STAGGER = 0, VDT_TB_TRUNC = 1 };
+/* column layout for vdt_bucketize: NHWC / [N, F] rows (t1, t2, t3 fc) or
+   NCHW sites with channel stride H*W (t3:70-90) */
+enum { VDT_LAYOUT_NHWC = 0, VDT_LAYOUT_NCHW = 1 };
+
+typedef struct {
+    int T;            /* TIME_WINDOW, or the truncated window T' */
+    int delta;        /* CHUNK: arrival-chunk width */
+    float fire_start; /* TIME_FIRE_START: inter-layer stagger (0 t1, 40 t2) */
+    float vth_init;   /* VTH_INIT */
+    float inf_time;   /* INF_TIME */
+    int lut_mode;     /* VDT_LUT_BY_TB | VDT_LUT_BY_TIN */
+    int decay_len;    /* LUT_decay length: T (t1:209) or T + 1 (t2:238) */
+    int lut_source;   /* VDT_LUT_DEVICE | VDT_LUT_HOST_LIBM */
+} vdt_time_cfg;
+
+typedef struct {
+    int kind;       /* VDT_CONV | VDT_FC */
+    int k;          /* square kernel size (conv; ignored for fc) */
+    int pad;        /* VDT_PAD_VALID | VDT_PAD_SAME */
+    int pool_after; /* 2x2 stride-2 min pool after this layer (k_pooling) */
+    int out;        /* VDT_OUT_FIRE | VDT_OUT_VMEM (last layer only) */
+} vdt_layer_desc;
+
+typedef struct {
+    int in_h, in_w, in_c; /* input map, NHWC */
+    float tc_in, td_in;   /* input encoding constants (t1:283, t2:335) */
+    int encoder;          /* applied when vdt_infer is given pixels */
+    int readout;          /* VDT_READ_* */
+} vdt_net_desc;
+
+const char* vdt_version(void);
+const char* vdt_strerror(int status);
+const char* vdt_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * Model: replaces load_weights (t1:185-206, t2:213-234) + the per-batch
+ * update_LUTs calls (t1:208-216, t2:236-243; tables are built once here).
+ * `blob` is the reference's weight-blob bytes; `layers` the topology that the
+ * reference's main hard-codes.  Shapes are checked against the blob.
+ * ---------------------------------------------------------------------- */
+int vdt_model_load_blob(const void* blob, size_t nbytes, const vdt_layer_desc* layers,
+                        int n_layers, const vdt_net_desc* net, const vdt_time_cfg* cfg,
+                        int device, vdt_model** out);
+void vdt_model_destroy(vdt_model* m);
+int vdt_model_info(const vdt_model* m, int* n_layers, int* n_classes, size_t* weight_bytes);
+/* copy layer `layer`'s tables to host: decay_len and T floats */
+int vdt_model_luts(const vdt_model* m, int layer, float* h_decay, float* h_th);
+
+/* ------------------------------------------------------------------------
+ * Context: workspace (activations, bucket lists) for batches <= max_batch,
+ * bound to one stream.  Replaces the reference's cudaMalloc'd g_bkt_* statics
+ * (t1:218-220, t2:245-248) and activation buffers.
+ * ---------------------------------------------------------------------- */
+int vdt_ctx_create(const vdt_model* m, int max_batch, vdt_stream stream, vdt_ctx** out);
+void vdt_ctx_destroy(vdt_ctx* c);
+/* 1 = launch the per-batch layer sequence as a captured CUDA graph (default) */
+int vdt_ctx_set_graphs(vdt_ctx* c, int enable);
+/* 1 = count events and fetched synapses (k_conv_bucketed's inner-loop
+   executions, as counted by task2 macs/stat_timesorted_macs.cu:136,155) */
+int vdt_ctx_set_counting(vdt_ctx* c, int enable);
+int vdt_ctx_counters(vdt_ctx* c, unsigned long long* events, unsigned long long* fetched);
+/* 1 = time every stage with CUDA events on the ctx stream (forces the eager,
+   non-graph path while on); vdt_ctx_layer_times then returns, per layer, the
+   milliseconds accumulated since the last read by its bucketize, integrate
+   (or membrane readout) and pool launches, and the number of batches run. */
+int vdt_ctx_set_profiling(vdt_ctx* c, int enable);
+int vdt_ctx_layer_times(vdt_ctx* c, int n_layers, float* bucketize_ms, float* integrate_ms,
+                        float* pool_ms, int* batches);
+
+/* ------------------------------------------------------------------------
+ * Whole-network inference: the per-batch body of the reference's main
+ * (t1:290-315, t2:341-392).  d_input is [batch, in_h, in_w, in_c]: spike
+ * times (input_is_pixels = 0) or pixels encoded with net->encoder.
+ * d_out receives the last layer's output [batch, classes] (first-spike times,
+ * or membrane values for a VDT_OUT_VMEM layer); d_pred (may be NULL) the
+ * readout.  Asynchronous on the ctx stream.
+ * ---------------------------------------------------------------------- */
+int vdt_infer(vdt_ctx* c, const float* d_input, int input_is_pixels, int batch,
+              float* d_out, int32_t* d_pred);
+/* Same, end to end from host buffers: H2D copy of the input, the network,
+   D2H copy of outputs; synchronous. */
+int vdt_infer_host(vdt_ctx* c, const float* h_input, int input_is_pixels, int batch,
+                   float* h_out, int32_t* h_pred);
+/* Same as vdt_infer, also writing every layer's output map (before its pool)
+   into d_layer_out[i] (device buffers sized [batch, H_out, W_out, C_out]). */
+int vdt_infer_trace(vdt_ctx* c, const float* d_input, int input_is_pixels, int batch,
+                    float* const* d_layer_out, float* d_out, int32_t* d_pred);
+
+/* ------------------------------------------------------------------------
+ * Per-stage entry points (the reference's kernels, as drop-ins)
+ * ---------------------------------------------------------------------- */
+
+/* update_LUTs (t1:208-216, t2:236-243) as a device kernel:
+   d_decay[t] = exp(-((float)t - td_integ) / tc_integ), t < decay_len;
+   d_th[t] = vth_init * exp(-((float)t - td_fire) / tc_fire), t < T. */
+int vdt_build_luts(int T, int decay_len, float tc_integ, float td_integ, float tc_fire,
+                   float td_fire, float vth_init, float* d_decay, float* d_th,
+                   vdt_stream stream);
+
+/* k_encode_image (t1:32-42, t2:32-42) / linear encoder; n elements. */
+int vdt_encode(const float* d_pixels, float* d_spikes, int64_t n, int encoder, float tc,
+               float td, int T, float inf_time, vdt_stream stream);
+
+/* k_bucketize (t1:45-80, t2:45-81), k_bucketize_conv / k_bucketize_fc
+   (t3:70-106): lossless counting sort of each column's spikes into
+   NC = ceil(T/delta) arrival chunks.  Output layout identical to the
+   reference: d_off [n_cols, NC+1] exclusive offsets (last = count),
+   d_cin / d_tin [n_cols, c_in] channel index and spike time, stable
+   (increasing channel) within each chunk.  NHWC: column col holds
+   d_in[col*c_in + i]; NCHW: col = n*hw + s holds d_in[n*c_in*hw + i*hw + s]. */
+int vdt_bucketize(const float* d_in, int64_t n_cols, int c_in, int layout, int64_t hw,
+                  const vdt_time_cfg* cfg, int tb_mode, int* d_off, int* d_cin,
+                  float* d_tin, vdt_stream stream);
+
+/* k_conv_bucketed (t1:83-162, t2:84-170): chunked early-exit integrator over
+   reference-layout buckets.  Weights HWIO [K, K, C_in, C_out] (conv) or
+   [C_in, C_out] (is_fc); output NHWC first-spike times [B, H_out, W_out,
+   C_out].  pad: taps at (h - pad + kh, w - pad + kw), out-of-range skipped. */
+int vdt_conv_bucketed(const int* d_off, const int* d_cin, const float* d_tin,
+                      const float* d_kernel, const float* d_bias, const float* d_decay,
+                      const float* d_th, int t_min, int B, int H_in, int W_in, int C_in,
+                      int H_out, int W_out, int C_out, int K, int pad, int is_fc,
+                      const vdt_time_cfg* cfg, float* d_out, vdt_stream stream);
+
+/* k_layer_vmem (t2:172-190): membrane readout of a non-firing last layer. */
+int vdt_layer_vmem(const float* d_in, const float* d_kernel, const float* d_bias,
+                   const float* d_decay, int B, int C_in, int C_out,
+                   const vdt_time_cfg* cfg, float* d_out, vdt_stream stream);
+
+/* k_pooling (t1:164-181, t2:192-209): 2x2 stride-2 min of spike times, NHWC. */
+int vdt_pool_min(const float* d_in, float* d_out, int B, int H_in, int W_in, int C,
+                 float inf_time, vdt_stream stream);
+
+/* host readout loops (t1:313-315, t2:391-392, t3:295-296) on the device */
+int vdt_readout(const float* d_out, int B, int K, int mode, float inf_time,
+                int32_t* d_pred, vdt_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VDTTFS_H */

@@ -1,0 +1,774 @@
+// runtime.cu -- host runtime of the engine and the C ABI (include/vdttfs.h).
+//
+//  * vdt_model: parses the reference's weight blob (load_weights, t1:185-206 /
+//    t2:213-234) against an explicit topology, uploads all weights into one
+//    device allocation and builds every layer's LUT pair once (the reference
+//    rebuilds them on the host and re-uploads them with blocking copies before
+//    every layer of every batch, t2:343-384).
+//  * vdt_ctx: the per-stream workspace (ping-pong activation maps, bucket
+//    lists) and a cache of captured CUDA graphs, one per (batch, input kind,
+//    counting) -- the reference synchronises the device after every launch
+//    (t2:260,273,280,286); here a batch is one graph launch.
+//  * the per-stage entry points wrap single kernels for drop-in use.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "vdt_internal.h"
+
+using namespace vdt;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    if (e == cudaErrorMemoryAllocation)
+        return fail(VDT_ERR_OOM, "%s: %s", what, cudaGetErrorString(e));
+    return fail(VDT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define VDT_CUDA(call)                                      \
+    do {                                                    \
+        cudaError_t e_ = (call);                            \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && (dev < 0 || cudaSetDevice(dev) == cudaSuccess))
+            ok = true;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+int check_cfg(const vdt_time_cfg* c) {
+    if (!c) return fail(VDT_ERR_INVALID, "time config is NULL");
+    if (c->T < 1 || c->T > 4096) return fail(VDT_ERR_INVALID, "T=%d out of range [1, 4096]", c->T);
+    if (c->delta < 1 || c->delta > 64)
+        return fail(VDT_ERR_INVALID, "delta=%d out of range [1, 64]", c->delta);
+    if (c->lut_mode != VDT_LUT_BY_TB && c->lut_mode != VDT_LUT_BY_TIN)
+        return fail(VDT_ERR_INVALID, "lut_mode=%d", c->lut_mode);
+    const int need = c->lut_mode == VDT_LUT_BY_TIN ? c->T + 1 : c->T;
+    if (c->decay_len < need)
+        return fail(VDT_ERR_INVALID, "decay_len=%d < %d required by lut_mode %d", c->decay_len,
+                    need, c->lut_mode);
+    if (c->lut_source != VDT_LUT_DEVICE && c->lut_source != VDT_LUT_HOST_LIBM)
+        return fail(VDT_ERR_INVALID, "lut_source=%d", c->lut_source);
+    return VDT_OK;
+}
+
+struct Layer {
+    vdt_layer_desc d;
+    int H_in, W_in, C_in, H_out, W_out, C_out;
+    float tc_fire, td;
+    int t_min;
+    float* W = nullptr;      // into the model's weight arena
+    float* bias = nullptr;
+    float* decay = nullptr;  // [decay_len]
+    float* th = nullptr;     // [T]
+};
+
+// Blob reader with bounds checks (the reference's load_weights has none).
+struct Reader {
+    const unsigned char* p;
+    size_t n, off = 0;
+    bool i32(int* v) {
+        if (off + 4 > n) return false;
+        memcpy(v, p + off, 4);
+        off += 4;
+        return true;
+    }
+    const float* f32(size_t count) {
+        if (count > (n - off) / 4) return nullptr;
+        const float* r = reinterpret_cast<const float*>(p + off);
+        off += 4 * count;
+        return r;
+    }
+};
+
+}  // namespace
+
+struct vdt_model {
+    int device = 0;
+    vdt_time_cfg cfg{};
+    vdt_net_desc net{};
+    std::vector<Layer> layers;
+    float* arena = nullptr;
+    size_t weight_bytes = 0;
+    int n_classes = 0;
+};
+
+struct GraphKey {
+    int batch, pixels, counting;
+    bool operator<(const GraphKey& o) const {
+        return std::tie(batch, pixels, counting) < std::tie(o.batch, o.pixels, o.counting);
+    }
+};
+
+struct vdt_ctx {
+    const vdt_model* m = nullptr;
+    int max_batch = 0;
+    cudaStream_t stream = nullptr;
+    float* act[3] = {nullptr, nullptr, nullptr};
+    float* in_slot = nullptr;    // [max_batch, in_h, in_w, in_c]
+    float* out_slot = nullptr;   // [max_batch, classes]
+    int32_t* pred_slot = nullptr;
+    int* off = nullptr;
+    int* cin = nullptr;
+    float* tin = nullptr;
+    unsigned long long* counters = nullptr;  // [events, fetched]
+    bool graphs = true;
+    bool counting = false;
+    bool profiling = false;
+    std::map<GraphKey, cudaGraphExec_t> cache;
+    // profiling: (layer, stage, start, stop) per timed launch, read back lazily
+    struct Mark { int layer, stage; cudaEvent_t a, b; };
+    std::vector<Mark> marks;
+    std::vector<cudaEvent_t> spare_events;
+    int prof_batches = 0;
+};
+
+namespace {
+cudaEvent_t take_event(vdt_ctx* c) {
+    if (!c->spare_events.empty()) {
+        cudaEvent_t e = c->spare_events.back();
+        c->spare_events.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+struct StageTimer {  // records a start/stop pair around one stage when profiling
+    vdt_ctx* c; int layer, stage; cudaEvent_t a = nullptr;
+    StageTimer(vdt_ctx* c_, int l, int s) : c(c_), layer(l), stage(s) {
+        if (c->profiling) { a = take_event(c); cudaEventRecord(a, c->stream); }
+    }
+    ~StageTimer() {
+        if (a) {
+            cudaEvent_t b = take_event(c);
+            cudaEventRecord(b, c->stream);
+            c->marks.push_back({layer, stage, a, b});
+        }
+    }
+};
+}  // namespace
+
+// ----------------------------------------------------------------- metadata
+extern "C" const char* vdt_version(void) { return "vdttfs-b200 0.1 (sm_100a)"; }
+
+extern "C" const char* vdt_strerror(int s) {
+    switch (s) {
+        case VDT_OK: return "ok";
+        case VDT_ERR_INVALID: return "invalid argument";
+        case VDT_ERR_BLOB: return "malformed weight blob";
+        case VDT_ERR_CUDA: return "CUDA error";
+        case VDT_ERR_OOM: return "out of device memory";
+        case VDT_ERR_UNSUPPORTED: return "unsupported configuration";
+        case VDT_ERR_CAPACITY: return "batch exceeds context capacity";
+        default: return "unknown status";
+    }
+}
+
+extern "C" const char* vdt_last_error(void) { return g_last_error.c_str(); }
+
+// -------------------------------------------------------------------- model
+static int host_luts(const vdt_time_cfg& c, float tci, float tdi, float tcf, float tdf,
+                     std::vector<float>& d, std::vector<float>& th) {
+    // update_LUTs' host loop (t1:210-213, t2:239-240), libm expf
+    d.resize(c.decay_len);
+    th.resize(c.T);
+    for (int t = 0; t < c.decay_len; ++t) d[t] = expf(-((float)t - tdi) / tci);
+    for (int t = 0; t < c.T; ++t) th[t] = c.vth_init * expf(-((float)t - tdf) / tcf);
+    return VDT_OK;
+}
+
+extern "C" int vdt_model_load_blob(const void* blob, size_t nbytes, const vdt_layer_desc* descs,
+                                   int n_layers, const vdt_net_desc* net, const vdt_time_cfg* cfg,
+                                   int device, vdt_model** out) {
+    g_last_error.clear();
+    if (!out) return fail(VDT_ERR_INVALID, "out is NULL");
+    *out = nullptr;
+    if (!blob || !descs || !net || n_layers <= 0)
+        return fail(VDT_ERR_INVALID, "blob/layers/net missing");
+    if (int s = check_cfg(cfg)) return s;
+    if (net->in_h <= 0 || net->in_w <= 0 || net->in_c <= 0)
+        return fail(VDT_ERR_INVALID, "bad input shape");
+    if (net->encoder < VDT_ENC_NONE || net->encoder > VDT_ENC_LINEAR)
+        return fail(VDT_ERR_INVALID, "encoder=%d", net->encoder);
+    if (net->readout < VDT_READ_ARGMIN_FIRST || net->readout > VDT_READ_ARGMAX)
+        return fail(VDT_ERR_INVALID, "readout=%d", net->readout);
+
+    Reader r{static_cast<const unsigned char*>(blob), nbytes};
+    int L;
+    if (!r.i32(&L)) return fail(VDT_ERR_BLOB, "blob shorter than its header");
+    if (L != n_layers) return fail(VDT_ERR_BLOB, "blob has %d layers, topology has %d", L, n_layers);
+
+    auto m = new vdt_model();
+    m->device = device;
+    m->cfg = *cfg;
+    m->net = *net;
+    std::vector<const float*> hk, hb;
+    int h = net->in_h, w = net->in_w, c = net->in_c;
+    for (int i = 0; i < L; ++i) {
+        Layer ly{};
+        ly.d = descs[i];
+        int nd;
+        if (!r.i32(&nd) || (nd != 2 && nd != 4)) { delete m; return fail(VDT_ERR_BLOB, "layer %d: kernel ndim", i); }
+        int shp[4] = {1, 1, 1, 1};
+        size_t ksz = 1;
+        for (int k = 0; k < nd; ++k) {
+            if (!r.i32(&shp[k]) || shp[k] <= 0) { delete m; return fail(VDT_ERR_BLOB, "layer %d: kernel shape", i); }
+            ksz *= (size_t)shp[k];
+        }
+        const float* kp = r.f32(ksz);
+        if (!kp) { delete m; return fail(VDT_ERR_BLOB, "layer %d: truncated kernel", i); }
+        int nb, bsz, tmp, tcs, tds;
+        if (!r.i32(&nb) || !r.i32(&bsz) || bsz <= 0) { delete m; return fail(VDT_ERR_BLOB, "layer %d: bias header", i); }
+        const float* bp = r.f32((size_t)bsz);
+        if (!bp) { delete m; return fail(VDT_ERR_BLOB, "layer %d: truncated bias", i); }
+        const float* tcp; const float* tdp;
+        if (!r.i32(&tmp) || !r.i32(&tcs) || tcs < 1 || !(tcp = r.f32((size_t)tcs)))
+            { delete m; return fail(VDT_ERR_BLOB, "layer %d: tc_fire", i); }
+        if (!r.i32(&tmp) || !r.i32(&tds) || tds < 1 || !(tdp = r.f32((size_t)tds)))
+            { delete m; return fail(VDT_ERR_BLOB, "layer %d: td", i); }
+        ly.tc_fire = tcp[0];
+        ly.td = tdp[0];
+        int t_min = (int)ceilf(ly.td);
+        ly.t_min = t_min < 0 ? 0 : t_min;
+        const bool last = (i == L - 1);
+        if (ly.d.out == VDT_OUT_VMEM && !last) { delete m; return fail(VDT_ERR_INVALID, "layer %d: VMEM output only on the last layer", i); }
+        if (ly.d.kind == VDT_CONV) {
+            if (nd != 4) { delete m; return fail(VDT_ERR_BLOB, "layer %d: conv needs an HWIO kernel", i); }
+            if (shp[0] != shp[1] || shp[0] != ly.d.k) { delete m; return fail(VDT_ERR_BLOB, "layer %d: kernel %dx%d, topology k=%d", i, shp[0], shp[1], ly.d.k); }
+            if (shp[2] != c) { delete m; return fail(VDT_ERR_BLOB, "layer %d: C_in %d, map has %d", i, shp[2], c); }
+            if (ly.d.out == VDT_OUT_VMEM) { delete m; return fail(VDT_ERR_UNSUPPORTED, "layer %d: VMEM readout on a conv", i); }
+            ly.H_in = h; ly.W_in = w; ly.C_in = c;
+            if (ly.d.pad == VDT_PAD_SAME) { ly.H_out = h; ly.W_out = w; }
+            else { ly.H_out = h - ly.d.k + 1; ly.W_out = w - ly.d.k + 1; }
+            if (ly.H_out <= 0 || ly.W_out <= 0) { delete m; return fail(VDT_ERR_INVALID, "layer %d: empty output map", i); }
+            ly.C_out = shp[3];
+        } else if (ly.d.kind == VDT_FC) {
+            const int f = h * w * c;
+            const int cin = nd == 2 ? shp[0] : shp[0] * shp[1] * shp[2];
+            if (cin != f) { delete m; return fail(VDT_ERR_BLOB, "layer %d: FC C_in %d, flattened map %d", i, cin, f); }
+            ly.H_in = ly.W_in = 1; ly.C_in = f;
+            ly.H_out = ly.W_out = 1; ly.C_out = shp[nd - 1];
+            ly.d.k = 1; ly.d.pad = VDT_PAD_VALID;
+            if (ly.d.pool_after) { delete m; return fail(VDT_ERR_INVALID, "layer %d: pool after FC", i); }
+        } else {
+            delete m; return fail(VDT_ERR_INVALID, "layer %d: kind %d", i, ly.d.kind);
+        }
+        if (bsz != ly.C_out) { delete m; return fail(VDT_ERR_BLOB, "layer %d: bias %d != C_out %d", i, bsz, ly.C_out); }
+        if (ly.d.out == VDT_OUT_FIRE &&
+            !integrate_supported(ly.d.kind == VDT_CONV ? ly.d.k : 1, ly.d.kind == VDT_FC, cfg->delta,
+                                 ly.C_out, cfg->T, cfg->decay_len)) {
+            delete m;
+            return fail(VDT_ERR_UNSUPPORTED, "layer %d: integrator needs delta in {1,2,4,...,64} and K*K <= 32", i);
+        }
+        if ((double)ly.d.k * ly.d.k * ly.C_in * ly.C_out >= 2147483647.0) {
+            delete m; return fail(VDT_ERR_UNSUPPORTED, "layer %d: kernel above 2^31 elements", i);
+        }
+        h = ly.H_out; w = ly.W_out; c = ly.C_out;
+        if (ly.d.pool_after) {
+            h /= 2; w /= 2;
+            if (h <= 0 || w <= 0) { delete m; return fail(VDT_ERR_INVALID, "layer %d: pool of a 1-wide map", i); }
+        }
+        m->layers.push_back(ly);
+        hk.push_back(kp);
+        hb.push_back(bp);
+    }
+    if (r.off != r.n) { delete m; return fail(VDT_ERR_BLOB, "blob has %zu trailing bytes", r.n - r.off); }
+    m->n_classes = m->layers.back().C_out;
+
+    DeviceGuard g(device);
+    if (!g.ok) { delete m; return fail(VDT_ERR_CUDA, "cannot select device %d", device); }
+    // one arena: weights, biases, LUT pairs (each segment 16-byte aligned)
+    auto al = [](size_t n) { return (n + 3) & ~size_t(3); };
+    size_t total = 0;
+    for (auto& ly : m->layers)
+        total += al((size_t)ly.d.k * ly.d.k * ly.C_in * ly.C_out) + al(ly.C_out) +
+                 al(cfg->decay_len) + al(cfg->T);
+    cudaError_t e = cudaMalloc(&m->arena, total * sizeof(float));
+    if (e != cudaSuccess) { delete m; return cuda_fail(e, "cudaMalloc(model arena)"); }
+    m->weight_bytes = total * sizeof(float);
+    float* cur = m->arena;
+    std::vector<LutJob> jobs;
+    std::vector<float> hd, hth;
+    for (size_t i = 0; i < m->layers.size(); ++i) {
+        Layer& ly = m->layers[i];
+        const size_t kn = (size_t)ly.d.k * ly.d.k * ly.C_in * ly.C_out;
+        ly.W = cur; cur += al(kn);
+        ly.bias = cur; cur += al(ly.C_out);
+        ly.decay = cur; cur += al(cfg->decay_len);
+        ly.th = cur; cur += al(cfg->T);
+        e = cudaMemcpy(ly.W, hk[i], kn * sizeof(float), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ly.bias, hb[i], ly.C_out * sizeof(float), cudaMemcpyHostToDevice);
+        const float tci = i ? m->layers[i - 1].tc_fire : net->tc_in;
+        const float tdi = i ? m->layers[i - 1].td : net->td_in;
+        if (e == cudaSuccess && cfg->lut_source == VDT_LUT_HOST_LIBM) {
+            host_luts(*cfg, tci, tdi, ly.tc_fire, ly.td, hd, hth);
+            e = cudaMemcpy(ly.decay, hd.data(), hd.size() * sizeof(float), cudaMemcpyHostToDevice);
+            if (e == cudaSuccess) e = cudaMemcpy(ly.th, hth.data(), hth.size() * sizeof(float), cudaMemcpyHostToDevice);
+        }
+        jobs.push_back(LutJob{tci, tdi, ly.tc_fire, ly.td, ly.decay, ly.th});
+        if (e != cudaSuccess) { cudaFree(m->arena); delete m; return cuda_fail(e, "weight upload"); }
+    }
+    if (cfg->lut_source == VDT_LUT_DEVICE) {
+        LutJob* dj = nullptr;
+        e = cudaMalloc(&dj, jobs.size() * sizeof(LutJob));
+        if (e == cudaSuccess) e = cudaMemcpy(dj, jobs.data(), jobs.size() * sizeof(LutJob), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = launch_build_luts(dj, (int)jobs.size(), cfg->T, cfg->decay_len, cfg->vth_init, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (dj) cudaFree(dj);
+        if (e != cudaSuccess) { cudaFree(m->arena); delete m; return cuda_fail(e, "LUT build"); }
+    }
+    *out = m;
+    return VDT_OK;
+}
+
+extern "C" void vdt_model_destroy(vdt_model* m) {
+    if (!m) return;
+    DeviceGuard g(m->device);
+    cudaFree(m->arena);
+    delete m;
+}
+
+extern "C" int vdt_model_info(const vdt_model* m, int* n_layers, int* n_classes, size_t* wbytes) {
+    if (!m) return fail(VDT_ERR_INVALID, "model is NULL");
+    if (n_layers) *n_layers = (int)m->layers.size();
+    if (n_classes) *n_classes = m->n_classes;
+    if (wbytes) *wbytes = m->weight_bytes;
+    return VDT_OK;
+}
+
+extern "C" int vdt_model_luts(const vdt_model* m, int layer, float* h_decay, float* h_th) {
+    if (!m || layer < 0 || layer >= (int)m->layers.size()) return fail(VDT_ERR_INVALID, "bad layer");
+    DeviceGuard g(m->device);
+    const Layer& ly = m->layers[layer];
+    if (h_decay) VDT_CUDA(cudaMemcpy(h_decay, ly.decay, m->cfg.decay_len * sizeof(float), cudaMemcpyDeviceToHost));
+    if (h_th) VDT_CUDA(cudaMemcpy(h_th, ly.th, m->cfg.T * sizeof(float), cudaMemcpyDeviceToHost));
+    return VDT_OK;
+}
+
+// ---------------------------------------------------------------------- ctx
+namespace {
+
+struct Sizes {
+    size_t act = 0, off = 0, bkt = 0;
+};
+
+Sizes ctx_sizes(const vdt_model* m, long long B) {
+    Sizes s;
+    const int OS = (m->cfg.T + m->cfg.delta - 1) / m->cfg.delta + 1;
+    s.act = (size_t)B * m->net.in_h * m->net.in_w * m->net.in_c;
+    for (auto& ly : m->layers) {
+        const size_t in = (size_t)B * ly.H_in * ly.W_in * ly.C_in;
+        const size_t out = (size_t)B * ly.H_out * ly.W_out * ly.C_out;
+        s.act = std::max(s.act, std::max(in, out));
+        if (ly.d.out == VDT_OUT_FIRE) {
+            const size_t cols = ly.d.kind == VDT_FC ? (size_t)B : (size_t)B * ly.H_in * ly.W_in;
+            s.off = std::max(s.off, cols * OS);
+            s.bkt = std::max(s.bkt, in);
+        }
+    }
+    return s;
+}
+
+void ctx_free(vdt_ctx* c) {
+    for (auto& mk : c->marks) { cudaEventDestroy(mk.a); cudaEventDestroy(mk.b); }
+    for (auto e : c->spare_events) cudaEventDestroy(e);
+    c->marks.clear();
+    c->spare_events.clear();
+    for (auto& kv : c->cache) cudaGraphExecDestroy(kv.second);
+    c->cache.clear();
+    for (auto& a : c->act) cudaFree(a);
+    cudaFree(c->in_slot); cudaFree(c->out_slot); cudaFree(c->pred_slot);
+    cudaFree(c->off); cudaFree(c->cin); cudaFree(c->tin); cudaFree(c->counters);
+}
+
+// Enqueue one batch: the reference's per-batch layer sequence.
+int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, int32_t* d_pred,
+            float* const* trace) {
+    const vdt_model* m = c->m;
+    const vdt_time_cfg& cfg = m->cfg;
+    const int NC = (cfg.T + cfg.delta - 1) / cfg.delta;
+    cudaStream_t s = c->stream;
+    const float* x = d_input;
+    int ai = 0;
+    if (pixels && m->net.encoder != VDT_ENC_NONE) {
+        const long long n = (long long)B * m->net.in_h * m->net.in_w * m->net.in_c;
+        VDT_CUDA(launch_encode(d_input, c->act[0], n, m->net.encoder, m->net.tc_in, m->net.td_in,
+                               cfg.T, cfg.inf_time, s));
+        x = c->act[0];
+        ai = 1;
+    }
+    unsigned long long* ev = c->counting ? c->counters : nullptr;
+    unsigned long long* fe = c->counting ? c->counters + 1 : nullptr;
+    const int L = (int)m->layers.size();
+    for (int i = 0; i < L; ++i) {
+        const Layer& ly = m->layers[i];
+        const bool last = i == L - 1;
+        float* y = (last && !ly.d.pool_after) ? d_out : c->act[ai];
+        if (trace && trace[i] && !last) y = trace[i];
+        if (trace && trace[i] && last && ly.d.pool_after) y = trace[i];
+        if (ly.d.out == VDT_OUT_VMEM) {
+            StageTimer st(c, i, 1);
+            VDT_CUDA(launch_layer_vmem(x, ly.W, ly.bias, ly.decay, B, ly.C_in, ly.C_out, cfg.T,
+                                       cfg.fire_start, cfg.inf_time, y, s));
+        } else {
+            const bool fc = ly.d.kind == VDT_FC;
+            BktParams bp{};
+            bp.in = x;
+            bp.n_cols = fc ? B : (long long)B * ly.H_in * ly.W_in;
+            bp.c_in = ly.C_in;
+            bp.layout = VDT_LAYOUT_NHWC;
+            bp.hw = 1;
+            bp.T = cfg.T; bp.delta = cfg.delta; bp.NC = NC;
+            bp.tfs = cfg.fire_start;
+            bp.tb_mode = VDT_TB_FLOOR_STAGGER;
+            bp.inf_time = cfg.inf_time;
+            bp.off = c->off; bp.cin = c->cin; bp.tin = c->tin;
+            bp.events = ev;
+            {
+                StageTimer st(c, i, 0);
+                VDT_CUDA(launch_bucketize(bp, s));
+            }
+            IntegParams ip{};
+            ip.off = c->off; ip.cin = c->cin; ip.tin = c->tin;
+            ip.W = ly.W; ip.bias = ly.bias; ip.lut_decay = ly.decay; ip.lut_th = ly.th;
+            ip.out = y;
+            ip.B = B; ip.H_in = ly.H_in; ip.W_in = ly.W_in; ip.C_in = ly.C_in;
+            ip.H_out = ly.H_out; ip.W_out = ly.W_out; ip.C_out = ly.C_out;
+            ip.K = ly.d.k;
+            ip.pad = (!fc && ly.d.pad == VDT_PAD_SAME) ? ly.d.k / 2 : 0;
+            ip.is_fc = fc;
+            ip.T = cfg.T; ip.delta = cfg.delta; ip.NC = NC; ip.t_min = ly.t_min;
+            ip.lut_mode = cfg.lut_mode; ip.decay_len = cfg.decay_len;
+            ip.tfs = cfg.fire_start; ip.inf_time = cfg.inf_time;
+            ip.fetched = fe;
+            StageTimer st(c, i, 1);
+            VDT_CUDA(launch_integrate(ip, s));
+        }
+        if (trace && trace[i] && y != trace[i])
+            VDT_CUDA(cudaMemcpyAsync(trace[i], y, (size_t)B * ly.H_out * ly.W_out * ly.C_out * sizeof(float),
+                                     cudaMemcpyDeviceToDevice, s));
+        x = y;
+        if (y == c->act[ai]) ai = (ai + 1) % 3;
+        if (ly.d.pool_after) {
+            float* z = last ? d_out : c->act[ai];
+            StageTimer st(c, i, 2);
+            VDT_CUDA(launch_pool_min(x, z, B, ly.H_out, ly.W_out, ly.C_out, cfg.inf_time, s));
+            x = z;
+            if (z == c->act[ai]) ai = (ai + 1) % 3;
+        }
+    }
+    if (d_pred)
+        VDT_CUDA(launch_readout(x, B, m->n_classes, m->net.readout, cfg.inf_time, d_pred, s));
+    if (c->profiling) c->prof_batches++;
+    return VDT_OK;
+}
+
+}  // namespace
+
+extern "C" int vdt_ctx_create(const vdt_model* m, int max_batch, vdt_stream stream, vdt_ctx** out) {
+    g_last_error.clear();
+    if (!out) return fail(VDT_ERR_INVALID, "out is NULL");
+    *out = nullptr;
+    if (!m || max_batch <= 0) return fail(VDT_ERR_INVALID, "model NULL or max_batch <= 0");
+    DeviceGuard g(m->device);
+    auto c = new vdt_ctx();
+    c->m = m;
+    c->max_batch = max_batch;
+    c->stream = static_cast<cudaStream_t>(stream);
+    const Sizes z = ctx_sizes(m, max_batch);
+    const size_t in_n = (size_t)max_batch * m->net.in_h * m->net.in_w * m->net.in_c;
+    cudaError_t e = cudaSuccess;
+    for (auto& a : c->act) if (e == cudaSuccess) e = cudaMalloc(&a, z.act * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->in_slot, in_n * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->out_slot, (size_t)max_batch * m->n_classes * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->pred_slot, (size_t)max_batch * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&c->off, std::max<size_t>(z.off, 1) * sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&c->cin, std::max<size_t>(z.bkt, 1) * sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&c->tin, std::max<size_t>(z.bkt, 1) * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->counters, 2 * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(c->counters, 0, 2 * sizeof(unsigned long long));
+    if (e != cudaSuccess) {
+        ctx_free(c);
+        delete c;
+        return cuda_fail(e, "ctx workspace allocation");
+    }
+    *out = c;
+    return VDT_OK;
+}
+
+extern "C" void vdt_ctx_destroy(vdt_ctx* c) {
+    if (!c) return;
+    DeviceGuard g(c->m->device);
+    if (c->stream) cudaStreamSynchronize(c->stream); else cudaDeviceSynchronize();
+    ctx_free(c);
+    delete c;
+}
+
+extern "C" int vdt_ctx_set_graphs(vdt_ctx* c, int enable) {
+    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    c->graphs = enable != 0;
+    return VDT_OK;
+}
+
+extern "C" int vdt_ctx_set_counting(vdt_ctx* c, int enable) {
+    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    c->counting = enable != 0;
+    return VDT_OK;
+}
+
+extern "C" int vdt_ctx_counters(vdt_ctx* c, unsigned long long* events, unsigned long long* fetched) {
+    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    DeviceGuard g(c->m->device);
+    unsigned long long h[2];
+    VDT_CUDA(cudaStreamSynchronize(c->stream));
+    VDT_CUDA(cudaMemcpy(h, c->counters, sizeof h, cudaMemcpyDeviceToHost));
+    if (events) *events = h[0];
+    if (fetched) *fetched = h[1];
+    VDT_CUDA(cudaMemset(c->counters, 0, sizeof h));
+    return VDT_OK;
+}
+
+extern "C" int vdt_ctx_set_profiling(vdt_ctx* c, int enable) {
+    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    c->profiling = enable != 0;
+    return VDT_OK;
+}
+
+extern "C" int vdt_ctx_layer_times(vdt_ctx* c, int n_layers, float* bkt_ms, float* int_ms,
+                                   float* pool_ms, int* batches) {
+    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    if (n_layers != (int)c->m->layers.size()) return fail(VDT_ERR_INVALID, "n_layers mismatch");
+    DeviceGuard g(c->m->device);
+    VDT_CUDA(cudaStreamSynchronize(c->stream));
+    float* dst[3] = {bkt_ms, int_ms, pool_ms};
+    for (auto* d : dst) if (d) for (int i = 0; i < n_layers; ++i) d[i] = 0.0f;
+    for (auto& mk : c->marks) {
+        float ms = 0.0f;
+        VDT_CUDA(cudaEventElapsedTime(&ms, mk.a, mk.b));
+        if (dst[mk.stage]) dst[mk.stage][mk.layer] += ms;
+        c->spare_events.push_back(mk.a);
+        c->spare_events.push_back(mk.b);
+    }
+    c->marks.clear();
+    if (batches) *batches = c->prof_batches;
+    c->prof_batches = 0;
+    return VDT_OK;
+}
+
+// Run one batch from ctx->in_slot into ctx->out_slot / pred_slot, through a
+// cached CUDA graph when enabled.
+static int run_slots(vdt_ctx* c, int pixels, int batch) {
+    if (!c->graphs || c->profiling) return enqueue(c, c->in_slot, pixels, batch, c->out_slot, c->pred_slot, nullptr);
+    const GraphKey key{batch, pixels, c->counting ? 1 : 0};
+    auto it = c->cache.find(key);
+    if (it == c->cache.end()) {
+        // capture on a private stream: the legacy default stream can't be captured
+        cudaStream_t cap;
+        VDT_CUDA(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+        cudaStream_t user = c->stream;
+        c->stream = cap;
+        cudaGraph_t graph = nullptr;
+        cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+        int st = VDT_OK;
+        if (e == cudaSuccess) st = enqueue(c, c->in_slot, pixels, batch, c->out_slot, c->pred_slot, nullptr);
+        cudaError_t e2 = cudaStreamEndCapture(cap, &graph);
+        c->stream = user;
+        cudaStreamDestroy(cap);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamBeginCapture");
+        if (st != VDT_OK) { if (graph) cudaGraphDestroy(graph); return st; }
+        if (e2 != cudaSuccess) return cuda_fail(e2, "cudaStreamEndCapture");
+        cudaGraphExec_t ex;
+        e = cudaGraphInstantiate(&ex, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+        it = c->cache.emplace(key, ex).first;
+    }
+    VDT_CUDA(cudaGraphLaunch(it->second, c->stream));
+    return VDT_OK;
+}
+
+static int check_batch(vdt_ctx* c, int batch) {
+    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    if (batch <= 0) return fail(VDT_ERR_INVALID, "batch=%d", batch);
+    if (batch > c->max_batch) return fail(VDT_ERR_CAPACITY, "batch %d > max_batch %d", batch, c->max_batch);
+    return VDT_OK;
+}
+
+extern "C" int vdt_infer(vdt_ctx* c, const float* d_input, int input_is_pixels, int batch,
+                         float* d_out, int32_t* d_pred) {
+    g_last_error.clear();
+    if (int s = check_batch(c, batch)) return s;
+    if (!d_input || !d_out) return fail(VDT_ERR_INVALID, "d_input/d_out is NULL");
+    DeviceGuard g(c->m->device);
+    const vdt_model* m = c->m;
+    const size_t in_n = (size_t)batch * m->net.in_h * m->net.in_w * m->net.in_c;
+    if (!c->graphs || c->profiling) return enqueue(c, d_input, input_is_pixels, batch, d_out, d_pred, nullptr);
+    VDT_CUDA(cudaMemcpyAsync(c->in_slot, d_input, in_n * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+    if (int s = run_slots(c, input_is_pixels, batch)) return s;
+    VDT_CUDA(cudaMemcpyAsync(d_out, c->out_slot, (size_t)batch * m->n_classes * sizeof(float),
+                             cudaMemcpyDeviceToDevice, c->stream));
+    if (d_pred)
+        VDT_CUDA(cudaMemcpyAsync(d_pred, c->pred_slot, (size_t)batch * sizeof(int32_t),
+                                 cudaMemcpyDeviceToDevice, c->stream));
+    return VDT_OK;
+}
+
+extern "C" int vdt_infer_host(vdt_ctx* c, const float* h_input, int input_is_pixels, int batch,
+                              float* h_out, int32_t* h_pred) {
+    g_last_error.clear();
+    if (int s = check_batch(c, batch)) return s;
+    if (!h_input) return fail(VDT_ERR_INVALID, "h_input is NULL");
+    DeviceGuard g(c->m->device);
+    const vdt_model* m = c->m;
+    const size_t in_n = (size_t)batch * m->net.in_h * m->net.in_w * m->net.in_c;
+    VDT_CUDA(cudaMemcpyAsync(c->in_slot, h_input, in_n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    if (c->graphs) {
+        if (int s = run_slots(c, input_is_pixels, batch)) return s;
+    } else {
+        if (int s = enqueue(c, c->in_slot, input_is_pixels, batch, c->out_slot, c->pred_slot, nullptr)) return s;
+    }
+    if (h_out)
+        VDT_CUDA(cudaMemcpyAsync(h_out, c->out_slot, (size_t)batch * m->n_classes * sizeof(float),
+                                 cudaMemcpyDeviceToHost, c->stream));
+    if (h_pred)
+        VDT_CUDA(cudaMemcpyAsync(h_pred, c->pred_slot, (size_t)batch * sizeof(int32_t),
+                                 cudaMemcpyDeviceToHost, c->stream));
+    VDT_CUDA(cudaStreamSynchronize(c->stream));
+    return VDT_OK;
+}
+
+extern "C" int vdt_infer_trace(vdt_ctx* c, const float* d_input, int input_is_pixels, int batch,
+                               float* const* d_layer_out, float* d_out, int32_t* d_pred) {
+    g_last_error.clear();
+    if (int s = check_batch(c, batch)) return s;
+    if (!d_input || !d_out || !d_layer_out) return fail(VDT_ERR_INVALID, "NULL buffer");
+    DeviceGuard g(c->m->device);
+    return enqueue(c, d_input, input_is_pixels, batch, d_out, d_pred, d_layer_out);
+}
+
+// ------------------------------------------------------- per-stage entries
+extern "C" int vdt_build_luts(int T, int decay_len, float tc_integ, float td_integ, float tc_fire,
+                              float td_fire, float vth_init, float* d_decay, float* d_th,
+                              vdt_stream stream) {
+    g_last_error.clear();
+    if (T < 1 || decay_len < 1 || !d_decay || !d_th) return fail(VDT_ERR_INVALID, "bad LUT arguments");
+    const LutJob j{tc_integ, td_integ, tc_fire, td_fire, d_decay, d_th};
+    VDT_CUDA(launch_build_lut_one(j, T, decay_len, vth_init, static_cast<cudaStream_t>(stream)));
+    return VDT_OK;
+}
+
+extern "C" int vdt_encode(const float* d_pixels, float* d_spikes, int64_t n, int encoder, float tc,
+                          float td, int T, float inf_time, vdt_stream stream) {
+    g_last_error.clear();
+    if (!d_pixels || !d_spikes || n < 0) return fail(VDT_ERR_INVALID, "bad encode arguments");
+    if (encoder != VDT_ENC_LOG && encoder != VDT_ENC_LINEAR) return fail(VDT_ERR_INVALID, "encoder=%d", encoder);
+    VDT_CUDA(launch_encode(d_pixels, d_spikes, n, encoder, tc, td, T, inf_time, static_cast<cudaStream_t>(stream)));
+    return VDT_OK;
+}
+
+extern "C" int vdt_bucketize(const float* d_in, int64_t n_cols, int c_in, int layout, int64_t hw,
+                             const vdt_time_cfg* cfg, int tb_mode, int* d_off, int* d_cin,
+                             float* d_tin, vdt_stream stream) {
+    g_last_error.clear();
+    if (int s = check_cfg(cfg)) return s;
+    if (!d_in || !d_off || !d_cin || !d_tin || n_cols < 0 || c_in <= 0)
+        return fail(VDT_ERR_INVALID, "bad bucketize arguments");
+    if (layout == VDT_LAYOUT_NCHW && (hw <= 0 || n_cols % hw != 0))
+        return fail(VDT_ERR_INVALID, "NCHW needs hw > 0 dividing n_cols");
+    if (tb_mode != VDT_TB_FLOOR_STAGGER && tb_mode != VDT_TB_TRUNC) return fail(VDT_ERR_INVALID, "tb_mode");
+    BktParams p{};
+    p.in = d_in; p.n_cols = n_cols; p.c_in = c_in; p.layout = layout; p.hw = hw < 1 ? 1 : hw;
+    p.T = cfg->T; p.delta = cfg->delta; p.NC = (cfg->T + cfg->delta - 1) / cfg->delta;
+    p.tfs = cfg->fire_start; p.tb_mode = tb_mode; p.inf_time = cfg->inf_time;
+    p.off = d_off; p.cin = d_cin; p.tin = d_tin; p.events = nullptr;
+    cudaError_t e = launch_bucketize(p, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue) return fail(VDT_ERR_UNSUPPORTED, "too many chunks for the counters");
+    VDT_CUDA(e);
+    return VDT_OK;
+}
+
+extern "C" int vdt_conv_bucketed(const int* d_off, const int* d_cin, const float* d_tin,
+                                 const float* d_kernel, const float* d_bias, const float* d_decay,
+                                 const float* d_th, int t_min, int B, int H_in, int W_in, int C_in,
+                                 int H_out, int W_out, int C_out, int K, int pad, int is_fc,
+                                 const vdt_time_cfg* cfg, float* d_out, vdt_stream stream) {
+    g_last_error.clear();
+    if (int s = check_cfg(cfg)) return s;
+    if (!d_off || !d_cin || !d_tin || !d_kernel || !d_bias || !d_decay || !d_th || !d_out)
+        return fail(VDT_ERR_INVALID, "NULL buffer");
+    if (B < 0 || C_in <= 0 || C_out <= 0 || (!is_fc && (H_out <= 0 || W_out <= 0 || K <= 0)))
+        return fail(VDT_ERR_INVALID, "bad shape");
+    if (!integrate_supported(K, is_fc, cfg->delta, C_out, cfg->T, cfg->decay_len))
+        return fail(VDT_ERR_UNSUPPORTED, "delta must be a power of two <= 64 and K*K <= 32");
+    IntegParams ip{};
+    ip.off = d_off; ip.cin = d_cin; ip.tin = d_tin;
+    ip.W = d_kernel; ip.bias = d_bias; ip.lut_decay = d_decay; ip.lut_th = d_th; ip.out = d_out;
+    ip.B = B; ip.H_in = is_fc ? 1 : H_in; ip.W_in = is_fc ? 1 : W_in; ip.C_in = C_in;
+    ip.H_out = is_fc ? 1 : H_out; ip.W_out = is_fc ? 1 : W_out; ip.C_out = C_out;
+    ip.K = is_fc ? 1 : K; ip.pad = is_fc ? 0 : pad; ip.is_fc = is_fc != 0;
+    ip.T = cfg->T; ip.delta = cfg->delta; ip.NC = (cfg->T + cfg->delta - 1) / cfg->delta;
+    ip.t_min = t_min; ip.lut_mode = cfg->lut_mode; ip.decay_len = cfg->decay_len;
+    ip.tfs = cfg->fire_start; ip.inf_time = cfg->inf_time; ip.fetched = nullptr;
+    VDT_CUDA(launch_integrate(ip, static_cast<cudaStream_t>(stream)));
+    return VDT_OK;
+}
+
+extern "C" int vdt_layer_vmem(const float* d_in, const float* d_kernel, const float* d_bias,
+                              const float* d_decay, int B, int C_in, int C_out,
+                              const vdt_time_cfg* cfg, float* d_out, vdt_stream stream) {
+    g_last_error.clear();
+    if (int s = check_cfg(cfg)) return s;
+    if (!d_in || !d_kernel || !d_bias || !d_decay || !d_out || B < 0 || C_in <= 0 || C_out <= 0)
+        return fail(VDT_ERR_INVALID, "bad vmem arguments");
+    cudaError_t e = launch_layer_vmem(d_in, d_kernel, d_bias, d_decay, B, C_in, C_out, cfg->T,
+                                      cfg->fire_start, cfg->inf_time, d_out, static_cast<cudaStream_t>(stream));
+    if (e == cudaErrorInvalidValue) return fail(VDT_ERR_UNSUPPORTED, "C_in too large for the vmem kernel");
+    VDT_CUDA(e);
+    return VDT_OK;
+}
+
+extern "C" int vdt_pool_min(const float* d_in, float* d_out, int B, int H_in, int W_in, int C,
+                            float inf_time, vdt_stream stream) {
+    g_last_error.clear();
+    if (!d_in || !d_out || B < 0 || H_in < 2 || W_in < 2 || C <= 0) return fail(VDT_ERR_INVALID, "bad pool arguments");
+    VDT_CUDA(launch_pool_min(d_in, d_out, B, H_in, W_in, C, inf_time, static_cast<cudaStream_t>(stream)));
+    return VDT_OK;
+}
+
+extern "C" int vdt_readout(const float* d_out, int B, int K, int mode, float inf_time, int32_t* d_pred,
+                           vdt_stream stream) {
+    g_last_error.clear();
+    if (!d_out || !d_pred || B < 0 || K <= 0) return fail(VDT_ERR_INVALID, "bad readout arguments");
+    if (mode < VDT_READ_ARGMIN_FIRST || mode > VDT_READ_ARGMAX) return fail(VDT_ERR_INVALID, "mode=%d", mode);
+    VDT_CUDA(launch_readout(d_out, B, K, mode, inf_time, d_pred, static_cast<cudaStream_t>(stream)));
+    return VDT_OK;
+}

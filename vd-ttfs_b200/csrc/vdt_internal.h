@@ -1,0 +1,69 @@
+// vdt_internal.h -- declarations shared by the engine's kernel files and the
+// host runtime (not part of the public ABI; see include/vdttfs.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "vdttfs.h"
+
+namespace vdt {
+
+// ---------------------------------------------------------------- bucketize
+struct BktParams {
+    const float* in;
+    long long n_cols;
+    int c_in;
+    int layout;        // VDT_LAYOUT_NHWC / VDT_LAYOUT_NCHW
+    long long hw;      // sites per image (NCHW)
+    int T, delta, NC;  // NC = ceil(T / delta)
+    float tfs;         // TIME_FIRE_START
+    int tb_mode;       // VDT_TB_FLOOR_STAGGER / VDT_TB_TRUNC
+    float inf_time;
+    int* off;          // [n_cols, NC + 1]
+    int* cin;          // [n_cols, c_in]
+    float* tin;        // [n_cols, c_in]
+    unsigned long long* events;  // optional event counter (may be null)
+};
+cudaError_t launch_bucketize(const BktParams& p, cudaStream_t s);
+
+// ---------------------------------------------------------------- integrate
+struct IntegParams {
+    const int* off;
+    const int* cin;
+    const float* tin;
+    const float* W;          // HWIO [K, K, C_in, C_out] or [C_in, C_out]
+    const float* bias;       // [C_out]
+    const float* lut_decay;  // [decay_len]
+    const float* lut_th;     // [T]
+    float* out;              // NHWC [B, H_out, W_out, C_out]
+    int B, H_in, W_in, C_in, H_out, W_out, C_out, K, pad, is_fc;
+    int T, delta, NC, t_min, lut_mode, decay_len;
+    float tfs, inf_time;
+    unsigned long long* fetched;  // optional synapse counter (may be null)
+};
+cudaError_t launch_integrate(const IntegParams& p, cudaStream_t s);
+// true when launch_integrate supports this (K, delta, C_out) combination
+bool integrate_supported(int K, int is_fc, int delta, int C_out, int T, int decay_len);
+
+// -------------------------------------------------------------- edges / LUT
+struct LutJob {            // one layer's table pair
+    float tc_integ, td_integ, tc_fire, td_fire;
+    float* decay;          // [decay_len]
+    float* th;             // [T]
+};
+cudaError_t launch_build_luts(const LutJob* d_jobs, int n_jobs, int T, int decay_len,
+                              float vth_init, cudaStream_t s);
+cudaError_t launch_build_lut_one(const LutJob& j, int T, int decay_len, float vth_init,
+                                 cudaStream_t s);
+cudaError_t launch_encode(const float* px, float* out, long long n, int encoder, float tc,
+                          float td, int T, float inf_time, cudaStream_t s);
+cudaError_t launch_pool_min(const float* in, float* out, int B, int H_in, int W_in, int C,
+                            float inf_time, cudaStream_t s);
+cudaError_t launch_layer_vmem(const float* in, const float* W, const float* bias,
+                              const float* lut_decay, int B, int C_in, int C_out, int T,
+                              float tfs, float inf_time, float* out, cudaStream_t s);
+cudaError_t launch_readout(const float* out, int B, int K, int mode, float inf_time,
+                           int32_t* pred, cudaStream_t s);
+
+}  // namespace vdt
