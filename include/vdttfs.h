@@ -117,6 +117,7 @@ int vdt_model_luts(const vdt_model* m, int layer, float* h_decay, float* h_th);
  * bound to one stream.  Replaces the reference's cudaMalloc'd g_bkt_* statics
  * (t1:218-220, t2:245-248) and activation buffers.
  * ---------------------------------------------------------------------- */
+/* The model must outlive every ctx created from it. */
 int vdt_ctx_create(const vdt_model* m, int max_batch, vdt_stream stream, vdt_ctx** out);
 void vdt_ctx_destroy(vdt_ctx* c);
 /* 1 = launch the per-batch layer sequence as a captured CUDA graph (default) */

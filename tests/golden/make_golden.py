@@ -10,6 +10,7 @@ Usage: python tests/golden/make_golden.py OUT_DIR
 """
 import os
 import sys
+import zlib
 
 import numpy as np
 
@@ -37,6 +38,23 @@ def times_i16(x):
     x = np.asarray(x, np.float32)
     assert np.all(x == np.round(x)) and x.max() <= 9999, "maps must hold integer spike times"
     return x.astype(np.int16)
+
+
+def crc(a):
+    return np.uint32(zlib.crc32(np.ascontiguousarray(a).tobytes()))
+
+
+def case_weights(task, i, C_in, C_out, K, is_fc):
+    """Weights of golden conv case i, regenerated from a fixed seed by the
+    test (tests/test_golden.py) instead of being stored."""
+    fan = C_in * (1 if is_fc else K * K)
+    shp = (C_in, C_out) if is_fc else (K, K, C_in, C_out)
+    r = np.random.default_rng(7000 + 100 * task + i)
+    return (r.standard_normal(shp, dtype=np.float32)
+            * np.float32(np.sqrt(2.0 / fan) * (1.3 if not is_fc else 1.0))).astype(np.float32)
+
+
+DVS_GAINS = [3.0, 3.0, 3.0, 1.0, 3.0, 3.0]
 
 
 def gen_task12(task, out):
@@ -71,9 +89,7 @@ def gen_task12(task, out):
                  (8, 1, 1, 256, 120, 1, 1), (8, 1, 1, 84, 10, 1, 1)]
     cv = {}
     for i, (B, H, W, C_in, C_out, K, is_fc) in enumerate(cases):
-        fan = C_in * (1 if is_fc else K * K)
-        shp = (C_in, C_out) if is_fc else (K, K, C_in, C_out)
-        Wt = (rng.standard_normal(shp) * np.sqrt(2.0 / fan) * (1.3 if not is_fc else 1.0)).astype(np.float32)
+        Wt = case_weights(task, i, C_in, C_out, K, is_fc)
         bias = (rng.standard_normal(C_out) * 0.05).astype(np.float32)
         x = spike_map(rng, (B, H, W, C_in), fire=0.35, T=80, edges=(i == 0))
         Ho, Wo = (H, W) if (task == 2 or is_fc) else (H - K + 1, W - K + 1)
@@ -82,7 +98,7 @@ def gen_task12(task, out):
         off, cin, tin = R.bucketize(T(x), n_cols, C_in)
         y = R.conv_bucketed(off, cin, tin, T(Wt), T(bias), d, t, 0, B, 1 if is_fc else H,
                             1 if is_fc else W, C_in, Ho, Wo, C_out, K, is_fc)
-        cv.update({f"x{i}": x, f"w{i}": Wt, f"b{i}": bias, f"y{i}": N(y),
+        cv.update({f"x{i}": x, f"wcrc{i}": crc(Wt), f"b{i}": bias, f"y{i}": N(y),
                    f"shape{i}": np.array([B, H, W, C_in, Ho, Wo, C_out, K, is_fc], np.int32)})
         cv[f"decay{i}"], cv[f"th{i}"] = N(d), N(t)
     np.savez_compressed(os.path.join(out, f"conv_t{task}.npz"), n=len(cases), T=Tw, chunk=R.chunk,
@@ -162,11 +178,11 @@ def gen_task3(out):
     rng = np.random.default_rng(303)
     Nn = 2
     frames = synth.dvs_frames(4, Nn, spec, density=0.05, stream=3)
-    wts = synth.dvs_weights(spec, 4, gains=[3.0, 3.0, 3.0, 1.0, 3.0, 3.0])
+    wts = synth.dvs_weights(spec, 4, gains=DVS_GAINS)
     maps = R.run(spec, wts, frames)
-    d = {"frames": frames, "decay_conv": R.decay_conv, "decay_fc": R.decay_fc,
-         "th_conv": R.th_conv, "th_fc": R.th_fc}
-    d.update({f"w_{k}": v for k, v in wts.items()})
+    d = {"frames": frames.astype(np.uint8), "decay_conv": R.decay_conv, "decay_fc": R.decay_fc,
+         "th_conv": R.th_conv, "th_fc": R.th_fc, "gains": np.array(DVS_GAINS, np.float32)}
+    d.update({f"wcrc_{k}": crc(v) for k, v in wts.items()})
     for i, m in enumerate(maps):
         d[f"map{i}"] = times_i16(m)
     # the generic kernels at non-reference shapes

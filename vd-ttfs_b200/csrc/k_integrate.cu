@@ -67,18 +67,121 @@ __device__ __forceinline__ void store_vec(float* p, const float (&r)[V]) {
     }
 }
 
+// cp.async of BYTES (4, 8 or 16) from global to shared memory, cached in L1
+// (weight rows are re-read by the other warps of the SM); src_bytes = 0
+// zero-fills without touching global memory.
+template <int BYTES>
+__device__ __forceinline__ void cp_async(float* smem, const float* gmem, int src_bytes) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;\n" ::"r"(sa), "l"(gmem), "n"(BYTES),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+constexpr int EB = 16;           // events staged per batch (per warp)
+constexpr int WARPS = 4;         // warps per CTA
+
+// Per-lane description of one event of the current batch.
+struct Ev {
+    int slot;    // tb - tau*DELTA, -1 = no event
+    int wo;      // weight row offset (tap*C_in + cin) * C_out
+    float lv;    // LUT_decay value
+};
+
+template <int DELTA>
+__device__ __forceinline__ Ev load_event(const IntegParams& p, int pidx, int total, const int* s_pre,
+                                         const int* s_st, int ntaps, long long img, int h_out, int w_out,
+                                         int base, const float* s_decay) {
+    Ev ev{-1, 0, 0.0f};
+    if (pidx >= total) return ev;
+    // tap holding flattened position pidx: last j with s_pre[j] <= pidx
+    int lo = 0, hi = ntaps - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_pre[mid] <= pidx) lo = mid; else hi = mid - 1;
+    }
+    const int j = lo;
+    long long col;
+    if (p.is_fc) {
+        col = img;
+    } else {
+        const int kh = j / p.K, kw = j - kh * p.K;
+        col = (img * p.H_in + (h_out - p.pad + kh)) * p.W_in + (w_out - p.pad + kw);
+    }
+    const int idx = s_st[j] + (pidx - s_pre[j]);
+    const long long at = col * p.C_in + idx;
+    const int ci = __ldg(p.cin + at);
+    const float t = __ldg(p.tin + at);
+    int tb = (int)floorf(t - p.tfs);
+    if (tb < 0) tb = 0;
+    int ti;
+    if (p.lut_mode == VDT_LUT_BY_TB) {
+        ti = tb;
+    } else {
+        ti = (int)t;
+        ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+    }
+    ev.slot = tb - base;
+    ev.lv = s_decay[ti];
+    ev.wo = ((p.is_fc ? 0 : j * p.C_in) + ci) * p.C_out;
+    return ev;
+}
+
+template <int V>
+__device__ __forceinline__ void stage_rows(float* buf, const Ev& ev, int n, const float* Wl, int lane,
+                                           bool lane_live) {
+    for (int q = 0; q < n; ++q) {
+        const int woq = __shfl_sync(FULL, ev.wo, q);
+        cp_async<4 * V>(buf + (q * 32 + lane) * V, Wl + (lane_live ? woq : 0), lane_live ? 4 * V : 0);
+    }
+    cp_async_commit();
+}
+
 template <int DELTA, int V>
-__global__ void __launch_bounds__(256, 2) k_integrate(IntegParams p, long long n_warps, int groups) {
-    extern __shared__ float s_lut[];
-    float* s_decay = s_lut;
-    float* s_th = s_lut + p.decay_len;
+__device__ __forceinline__ void apply_batch(float (&d)[DELTA][V], const float* buf, const Ev& ev, int lane) {
+#pragma unroll
+    for (int sl = 0; sl < DELTA; ++sl) {
+        unsigned m = __ballot_sync(FULL, ev.slot == sl);
+        while (m) {
+            const int q = __ffs(m) - 1;
+            m &= m - 1;
+            const float lq = __shfl_sync(FULL, ev.lv, q);
+            const float* w = buf + (q * 32 + lane) * V;
+            if constexpr (V == 4) {
+                const float4 x = *reinterpret_cast<const float4*>(w);
+                d[sl][0] = fmaf(x.x, lq, d[sl][0]);
+                d[sl][1] = fmaf(x.y, lq, d[sl][1]);
+                d[sl][2] = fmaf(x.z, lq, d[sl][2]);
+                d[sl][3] = fmaf(x.w, lq, d[sl][3]);
+            } else if constexpr (V == 2) {
+                const float2 x = *reinterpret_cast<const float2*>(w);
+                d[sl][0] = fmaf(x.x, lq, d[sl][0]);
+                d[sl][1] = fmaf(x.y, lq, d[sl][1]);
+            } else {
+                d[sl][0] = fmaf(w[0], lq, d[sl][0]);
+            }
+        }
+    }
+}
+
+template <int DELTA, int V>
+__global__ void __launch_bounds__(WARPS * 32, 3) k_integrate(IntegParams p, long long n_warps, int groups) {
+    extern __shared__ __align__(16) float smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* stage = smem + warp * (2 * EB * 32 * V);           // [2][EB][32][V]
+    int* s_pre = reinterpret_cast<int*>(smem + WARPS * 2 * EB * 32 * V) + warp * 64;
+    int* s_st = s_pre + 32;
+    float* s_decay = reinterpret_cast<float*>(reinterpret_cast<int*>(smem + WARPS * 2 * EB * 32 * V) + WARPS * 64);
+    float* s_th = s_decay + p.decay_len;
     for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
     for (int i = threadIdx.x; i < p.T; i += blockDim.x) s_th[i] = p.lut_th[i];
     __syncthreads();
 
-    const int lane = threadIdx.x & 31;
-    const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (gw >= n_warps) return;                        // warp-uniform
+    const long long gw = (long long)blockIdx.x * WARPS + warp;
+    if (gw >= n_warps) return;                                // warp-uniform
     const long long pix = gw / groups;
     const int grp = (int)(gw - pix * groups);
     const int c0 = (grp * 32 + lane) * V;
@@ -96,15 +199,15 @@ __global__ void __launch_bounds__(256, 2) k_integrate(IntegParams p, long long n
     const int OS = p.NC + 1;
 
     // lane j < ntaps owns tap j's input column (or none if out of range)
-    long long my_col = -1;
+    const int* my_off = nullptr;
     if (lane < ntaps) {
         if (p.is_fc) {
-            my_col = img;
+            my_off = p.off + img * OS;
         } else {
             const int kh = lane / p.K, kw = lane - (lane / p.K) * p.K;
             const int h_in = h_out - p.pad + kh, w_in = w_out - p.pad + kw;
             if (h_in >= 0 && h_in < p.H_in && w_in >= 0 && w_in < p.W_in)
-                my_col = (img * p.H_in + h_in) * p.W_in + w_in;
+                my_off = p.off + ((img * p.H_in + h_in) * p.W_in + w_in) * OS;
         }
     }
 
@@ -119,8 +222,26 @@ __global__ void __launch_bounds__(256, 2) k_integrate(IntegParams p, long long n
     unsigned long long fetched = 0;
     const float* Wl = p.W + (lane_ok ? c0 : 0);
 
+    // chunk offsets one chunk ahead
+    int nx_s = 0, nx_e = 0;
+    if (my_off) { nx_s = __ldg(my_off); nx_e = __ldg(my_off + 1); }
+
     for (int tau = 0; tau < p.NC; ++tau) {
         const int base = tau * DELTA;
+        const int my_s = nx_s, cnt = nx_e - nx_s;
+        if (my_off && tau + 1 < p.NC) { nx_s = __ldg(my_off + tau + 1); nx_e = __ldg(my_off + tau + 2); }
+
+        // flatten the taps' events of this chunk into one list, tap order kept
+        int inc = cnt;
+#pragma unroll
+        for (int dd = 1; dd < 32; dd <<= 1) {
+            const int u = __shfl_up_sync(FULL, inc, dd);
+            if (lane >= dd) inc += u;
+        }
+        const int total = __shfl_sync(FULL, inc, 31);
+        if (lane < ntaps) { s_pre[lane] = inc - cnt; s_st[lane] = my_s; }
+        __syncwarp();
+
         float d[DELTA][V];
 #pragma unroll
         for (int i = 0; i < DELTA; ++i)
@@ -131,62 +252,34 @@ __global__ void __launch_bounds__(256, 2) k_integrate(IntegParams p, long long n
 #pragma unroll
         for (int v = 0; v < V; ++v) n_live += alive[v] ? 1 : 0;
         const bool lane_live = n_live > 0;
+        if (p.fetched) fetched += (unsigned long long)total * n_live;
 
-        int my_s = 0, my_e = 0;
-        if (my_col >= 0) {
-            const int* o = p.off + my_col * OS + tau;
-            my_s = __ldg(o);
-            my_e = __ldg(o + 1);
-        }
-        for (int j = 0; j < ntaps; ++j) {
-            const int s = __shfl_sync(FULL, my_s, j);
-            const int e = __shfl_sync(FULL, my_e, j);
-            if (s >= e) continue;                     // warp-uniform
-            const long long col = p.is_fc ? img
-                : (img * p.H_in + (h_out - p.pad + j / p.K)) * p.W_in + (w_out - p.pad + j % p.K);
-            const int wrow0 = p.is_fc ? 0 : j * p.C_in;
-            const int* bc = p.cin + col * p.C_in;
-            const float* bt = p.tin + col * p.C_in;
-            for (int p0 = s; p0 < e; p0 += 32) {
-                const int idx = p0 + lane;
-                int slot = -1, wo = 0;
-                float lv = 0.0f;
-                if (idx < e) {
-                    const int ci = __ldg(bc + idx);
-                    const float t = __ldg(bt + idx);
-                    int tb = (int)floorf(t - p.tfs);
-                    if (tb < 0) tb = 0;
-                    int ti;
-                    if (p.lut_mode == VDT_LUT_BY_TB) {
-                        ti = tb;
-                    } else {
-                        ti = (int)t;
-                        ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
-                    }
-                    slot = tb - base;
-                    lv = s_decay[ti];
-                    wo = (wrow0 + ci) * p.C_out;
+        if (total > 0) {
+            // batch pipeline: rows of batch b+1 are in flight while b is applied
+            Ev cur = load_event<DELTA>(p, lane < EB ? lane : total, total, s_pre, s_st, ntaps, img,
+                                       h_out, w_out, base, s_decay);
+            int ncur = min(EB, total);
+            stage_rows<V>(stage, cur, ncur, Wl, lane, lane_live);
+            int buf = 0;
+            for (int b0 = 0; b0 < total; b0 += EB) {
+                const int nb0 = b0 + EB;
+                Ev nxt{-1, 0, 0.0f};
+                int nnext = 0;
+                if (nb0 < total) {
+                    nnext = min(EB, total - nb0);
+                    nxt = load_event<DELTA>(p, lane < EB ? nb0 + lane : total, total, s_pre, s_st, ntaps,
+                                            img, h_out, w_out, base, s_decay);
+                    stage_rows<V>(stage + (buf ^ 1) * EB * 32 * V, nxt, nnext, Wl, lane, lane_live);
+                    cp_async_wait<1>();
+                } else {
+                    cp_async_wait<0>();
                 }
-                if (p.fetched) fetched += (unsigned long long)__popc(__ballot_sync(FULL, idx < e)) * n_live;
-#pragma unroll
-                for (int sl = 0; sl < DELTA; ++sl) {
-                    unsigned m = __ballot_sync(FULL, slot == sl);
-                    while (m) {
-                        const int q = __ffs(m) - 1;
-                        m &= m - 1;
-                        const int woq = __shfl_sync(FULL, wo, q);
-                        const float lq = __shfl_sync(FULL, lv, q);
-                        float w[V];
-                        if (lane_live) {
-                            load_vec<V>(Wl + woq, w);
-                        } else {
-#pragma unroll
-                            for (int v = 0; v < V; ++v) w[v] = 0.0f;
-                        }
-#pragma unroll
-                        for (int v = 0; v < V; ++v) d[sl][v] = fmaf(w[v], lq, d[sl][v]);
-                    }
-                }
+                __syncwarp();
+                apply_batch<DELTA, V>(d, stage + buf * EB * 32 * V, cur, lane);
+                __syncwarp();
+                cur = nxt;
+                ncur = nnext;
+                buf ^= 1;
             }
         }
         // integrate this chunk; first crossing wins (t1:150-157, t2:158-165)
@@ -228,6 +321,20 @@ int pick_v(int C_out, int delta) {
     return 1;
 }
 
+template <int DELTA, int V>
+cudaError_t launch_dv(const IntegParams& p, cudaStream_t s, long long n_warps, int groups) {
+    const long long blocks = (n_warps + WARPS - 1) / WARPS;
+    const size_t smem = (size_t)WARPS * 2 * EB * 32 * V * sizeof(float) + WARPS * 64 * sizeof(int) +
+                        (size_t)(p.decay_len + p.T) * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k_integrate<DELTA, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    k_integrate<DELTA, V><<<(unsigned)blocks, WARPS * 32, smem, s>>>(p, n_warps, groups);
+    return cudaGetLastError();
+}
+
 template <int DELTA>
 cudaError_t launch_delta(const IntegParams& p, cudaStream_t s) {
     const int V = pick_v(p.C_out, DELTA);
@@ -235,15 +342,11 @@ cudaError_t launch_delta(const IntegParams& p, cudaStream_t s) {
     const long long pixels = p.is_fc ? (long long)p.B : (long long)p.B * p.H_out * p.W_out;
     const long long n_warps = pixels * groups;
     if (n_warps <= 0) return cudaSuccess;
-    const int warps_per_cta = 8;
-    const long long blocks = (n_warps + warps_per_cta - 1) / warps_per_cta;
-    const size_t smem = (size_t)(p.decay_len + p.T) * sizeof(float);
     switch (V) {
-        case 4: k_integrate<DELTA, (DELTA <= 16 ? 4 : 1)><<<(unsigned)blocks, 256, smem, s>>>(p, n_warps, groups); break;
-        case 2: k_integrate<DELTA, (DELTA <= 32 ? 2 : 1)><<<(unsigned)blocks, 256, smem, s>>>(p, n_warps, groups); break;
-        default: k_integrate<DELTA, 1><<<(unsigned)blocks, 256, smem, s>>>(p, n_warps, groups); break;
+        case 4: return launch_dv<DELTA, (DELTA <= 16 ? 4 : 1)>(p, s, n_warps, groups);
+        case 2: return launch_dv<DELTA, (DELTA <= 32 ? 2 : 1)>(p, s, n_warps, groups);
+        default: return launch_dv<DELTA, 1>(p, s, n_warps, groups);
     }
-    return cudaGetLastError();
 }
 
 }  // namespace
@@ -252,7 +355,7 @@ bool integrate_supported(int K, int is_fc, int delta, int C_out, int T, int deca
     if (!is_fc && (K < 1 || K * K > 32)) return false;
     if (delta != 1 && delta != 2 && delta != 4 && delta != 8 && delta != 16 && delta != 32 && delta != 64)
         return false;
-    if ((size_t)(decay_len + T) * sizeof(float) > 48 * 1024) return false;
+    if ((size_t)(decay_len + T) * sizeof(float) > 64 * 1024) return false;
     return C_out > 0;
 }
 

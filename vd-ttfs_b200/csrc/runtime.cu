@@ -56,8 +56,13 @@ struct DeviceGuard {
     int prev = -1;
     bool ok = false;
     explicit DeviceGuard(int dev) {
-        if (cudaGetDevice(&prev) == cudaSuccess && (dev < 0 || cudaSetDevice(dev) == cudaSuccess))
-            ok = true;
+        if (cudaGetDevice(&prev) != cudaSuccess) {
+            prev = -1;
+            cudaGetLastError();  // leave no error behind for other libraries
+            return;
+        }
+        if (dev < 0 || cudaSetDevice(dev) == cudaSuccess) ok = true;
+        else cudaGetLastError();
     }
     ~DeviceGuard() {
         if (prev >= 0) cudaSetDevice(prev);
@@ -129,7 +134,8 @@ struct GraphKey {
 };
 
 struct vdt_ctx {
-    const vdt_model* m = nullptr;
+    const vdt_model* m = nullptr;  // must outlive the ctx
+    int device = 0;
     int max_batch = 0;
     cudaStream_t stream = nullptr;
     float* act[3] = {nullptr, nullptr, nullptr};
@@ -502,6 +508,7 @@ extern "C" int vdt_ctx_create(const vdt_model* m, int max_batch, vdt_stream stre
     DeviceGuard g(m->device);
     auto c = new vdt_ctx();
     c->m = m;
+    c->device = m->device;
     c->max_batch = max_batch;
     c->stream = static_cast<cudaStream_t>(stream);
     const Sizes z = ctx_sizes(m, max_batch);
@@ -527,7 +534,7 @@ extern "C" int vdt_ctx_create(const vdt_model* m, int max_batch, vdt_stream stre
 
 extern "C" void vdt_ctx_destroy(vdt_ctx* c) {
     if (!c) return;
-    DeviceGuard g(c->m->device);
+    DeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream); else cudaDeviceSynchronize();
     ctx_free(c);
     delete c;

@@ -23,6 +23,7 @@ Device tensors are torch CUDA tensors; torch provides memory and streams only.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -80,6 +81,7 @@ class Model:
         check(lib().vdt_model_info(h, C.byref(nl), C.byref(nc), C.byref(wb)), "vdt_model_info")
         self.n_classes = nc.value
         self.weight_bytes = wb.value
+        self._contexts = weakref.WeakSet()   # closed before the model goes
 
     def luts(self, layer: int):
         d = np.zeros(self.net.decay_len, np.float32)
@@ -89,6 +91,8 @@ class Model:
 
     def close(self):
         if self.h:
+            for c in list(self._contexts):
+                c.close()
             lib().vdt_model_destroy(self.h)
             self.h = None
 
@@ -110,6 +114,7 @@ class Context:
         check(lib().vdt_ctx_create(model.h, max_batch, C.c_void_p(self.stream), C.byref(h)),
               "vdt_ctx_create")
         self.h = h
+        model._contexts.add(self)
         self.set_graphs(graphs)
 
     def set_graphs(self, on: bool):
