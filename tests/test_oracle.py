@@ -169,3 +169,21 @@ def test_dvs_conv_delta_invariant(O, delta):
     y, _, _ = O.dvs_conv(x, w, 2, 8, 5, 6, 6, spec)
     y32, _, _ = O.dvs_conv(x, w, 2, 8, 5, 6, 6, nets.dvs_ref(delta=32))
     assert bits_equal(y, y32)
+
+
+@pytest.mark.parametrize("delta,tfs", [(4, 40.0), (8, 40.0), (16, 0.0), (32, 0.0), (64, 40.0)])
+def test_time_sorted_buckets_refine_the_chunk_buckets(O, delta, tfs):
+    """The fused path sorts at delta = 1; its offsets at multiples of delta are
+    the reference's chunk offsets, and each chunk holds the same events."""
+    rng = np.random.default_rng(delta)
+    x = spike_map(rng, (300, 45), fire=0.5, T=80, edges=True)
+    off, cin, tin, n = O.bucketize(x, 300, 45, 80, delta, tfs, 0)
+    fo, fc, ft, n1 = O.bucketize(x, 300, 45, 80, 1, tfs, 0)
+    assert n == n1
+    nc = (80 + delta - 1) // delta
+    idx = [min(c * delta, 80) for c in range(nc)] + [80]
+    assert np.array_equal(off, fo[:, idx])
+    for c in range(300):
+        for ch in range(nc):
+            a, b = off[c, ch], off[c, ch + 1]
+            assert sorted(cin[c, a:b]) == sorted(fc[c, a:b])

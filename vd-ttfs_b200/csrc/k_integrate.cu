@@ -67,121 +67,95 @@ __device__ __forceinline__ void store_vec(float* p, const float (&r)[V]) {
     }
 }
 
-// cp.async of BYTES (4, 8 or 16) from global to shared memory, cached in L1
-// (weight rows are re-read by the other warps of the SM); src_bytes = 0
-// zero-fills without touching global memory.
-template <int BYTES>
-__device__ __forceinline__ void cp_async(float* smem, const float* gmem, int src_bytes) {
-    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;\n" ::"r"(sa), "l"(gmem), "n"(BYTES),
-                 "r"(src_bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
-
-constexpr int EB = 16;           // events staged per batch (per warp)
 constexpr int WARPS = 4;         // warps per CTA
 
-// Per-lane description of one event of the current batch.
-struct Ev {
-    int slot;    // tb - tau*DELTA, -1 = no event
-    int wo;      // weight row offset (tap*C_in + cin) * C_out
-    float lv;    // LUT_decay value
-};
-
-template <int DELTA>
-__device__ __forceinline__ Ev load_event(const IntegParams& p, int pidx, int total, const int* s_pre,
-                                         const int* s_st, int ntaps, long long img, int h_out, int w_out,
-                                         int base, const float* s_decay) {
-    Ev ev{-1, 0, 0.0f};
-    if (pidx >= total) return ev;
-    // tap holding flattened position pidx: last j with s_pre[j] <= pidx
-    int lo = 0, hi = ntaps - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (s_pre[mid] <= pidx) lo = mid; else hi = mid - 1;
-    }
-    const int j = lo;
-    long long col;
-    if (p.is_fc) {
-        col = img;
-    } else {
-        const int kh = j / p.K, kw = j - kh * p.K;
-        col = (img * p.H_in + (h_out - p.pad + kh)) * p.W_in + (w_out - p.pad + kw);
-    }
-    const int idx = s_st[j] + (pidx - s_pre[j]);
-    const long long at = col * p.C_in + idx;
-    const int ci = __ldg(p.cin + at);
-    const float t = __ldg(p.tin + at);
-    int tb = (int)floorf(t - p.tfs);
-    if (tb < 0) tb = 0;
-    int ti;
-    if (p.lut_mode == VDT_LUT_BY_TB) {
-        ti = tb;
-    } else {
-        ti = (int)t;
-        ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
-    }
-    ev.slot = tb - base;
-    ev.lv = s_decay[ti];
-    ev.wo = ((p.is_fc ? 0 : j * p.C_in) + ci) * p.C_out;
-    return ev;
-}
-
-template <int V>
-__device__ __forceinline__ void stage_rows(float* buf, const Ev& ev, int n, const float* Wl, int lane,
-                                           bool lane_live) {
-    for (int q = 0; q < n; ++q) {
-        const int woq = __shfl_sync(FULL, ev.wo, q);
-        cp_async<4 * V>(buf + (q * 32 + lane) * V, Wl + (lane_live ? woq : 0), lane_live ? 4 * V : 0);
-    }
-    cp_async_commit();
+// delta[slot][*] = fma(w[*], lv, delta[slot][*]) for a warp-uniform slot in
+// [0, DELTA): a switch over exactly DELTA cases keeps every delta index a
+// compile-time constant, so delta[][] lives in registers.
+template <int DELTA, int V, int S>
+__device__ __forceinline__ void add_case(float (&d)[DELTA][V], const float (&w)[V], float lv) {
+#pragma unroll
+    for (int v = 0; v < V; ++v) d[S][v] = fmaf(w[v], lv, d[S][v]);
 }
 
 template <int DELTA, int V>
-__device__ __forceinline__ void apply_batch(float (&d)[DELTA][V], const float* buf, const Ev& ev, int lane) {
-#pragma unroll
-    for (int sl = 0; sl < DELTA; ++sl) {
-        unsigned m = __ballot_sync(FULL, ev.slot == sl);
-        while (m) {
-            const int q = __ffs(m) - 1;
-            m &= m - 1;
-            const float lq = __shfl_sync(FULL, ev.lv, q);
-            const float* w = buf + (q * 32 + lane) * V;
-            if constexpr (V == 4) {
-                const float4 x = *reinterpret_cast<const float4*>(w);
-                d[sl][0] = fmaf(x.x, lq, d[sl][0]);
-                d[sl][1] = fmaf(x.y, lq, d[sl][1]);
-                d[sl][2] = fmaf(x.z, lq, d[sl][2]);
-                d[sl][3] = fmaf(x.w, lq, d[sl][3]);
-            } else if constexpr (V == 2) {
-                const float2 x = *reinterpret_cast<const float2*>(w);
-                d[sl][0] = fmaf(x.x, lq, d[sl][0]);
-                d[sl][1] = fmaf(x.y, lq, d[sl][1]);
-            } else {
-                d[sl][0] = fmaf(w[0], lq, d[sl][0]);
-            }
+__device__ __forceinline__ void add_event(float (&d)[DELTA][V], int slot, const float (&w)[V], float lv) {
+#define VDT_C(S) case S: if constexpr (S < DELTA) add_case<DELTA, V, S>(d, w, lv); break;
+    if constexpr (DELTA <= 8) {
+        switch (slot) { VDT_C(0) VDT_C(1) VDT_C(2) VDT_C(3) VDT_C(4) VDT_C(5) VDT_C(6) VDT_C(7) default: break; }
+    } else if constexpr (DELTA <= 16) {
+        switch (slot) {
+            VDT_C(0) VDT_C(1) VDT_C(2) VDT_C(3) VDT_C(4) VDT_C(5) VDT_C(6) VDT_C(7)
+            VDT_C(8) VDT_C(9) VDT_C(10) VDT_C(11) VDT_C(12) VDT_C(13) VDT_C(14) VDT_C(15) default: break;
+        }
+    } else if constexpr (DELTA <= 32) {
+        switch (slot) {
+            VDT_C(0) VDT_C(1) VDT_C(2) VDT_C(3) VDT_C(4) VDT_C(5) VDT_C(6) VDT_C(7)
+            VDT_C(8) VDT_C(9) VDT_C(10) VDT_C(11) VDT_C(12) VDT_C(13) VDT_C(14) VDT_C(15)
+            VDT_C(16) VDT_C(17) VDT_C(18) VDT_C(19) VDT_C(20) VDT_C(21) VDT_C(22) VDT_C(23)
+            VDT_C(24) VDT_C(25) VDT_C(26) VDT_C(27) VDT_C(28) VDT_C(29) VDT_C(30) VDT_C(31) default: break;
+        }
+    } else {
+        switch (slot) {
+            VDT_C(0) VDT_C(1) VDT_C(2) VDT_C(3) VDT_C(4) VDT_C(5) VDT_C(6) VDT_C(7)
+            VDT_C(8) VDT_C(9) VDT_C(10) VDT_C(11) VDT_C(12) VDT_C(13) VDT_C(14) VDT_C(15)
+            VDT_C(16) VDT_C(17) VDT_C(18) VDT_C(19) VDT_C(20) VDT_C(21) VDT_C(22) VDT_C(23)
+            VDT_C(24) VDT_C(25) VDT_C(26) VDT_C(27) VDT_C(28) VDT_C(29) VDT_C(30) VDT_C(31)
+            VDT_C(32) VDT_C(33) VDT_C(34) VDT_C(35) VDT_C(36) VDT_C(37) VDT_C(38) VDT_C(39)
+            VDT_C(40) VDT_C(41) VDT_C(42) VDT_C(43) VDT_C(44) VDT_C(45) VDT_C(46) VDT_C(47)
+            VDT_C(48) VDT_C(49) VDT_C(50) VDT_C(51) VDT_C(52) VDT_C(53) VDT_C(54) VDT_C(55)
+            VDT_C(56) VDT_C(57) VDT_C(58) VDT_C(59) VDT_C(60) VDT_C(61) VDT_C(62) VDT_C(63) default: break;
         }
     }
+#undef VDT_C
 }
 
-template <int DELTA, int V>
-__global__ void __launch_bounds__(WARPS * 32, 3) k_integrate(IntegParams p, long long n_warps, int groups) {
-    extern __shared__ __align__(16) float smem[];
+// Per-warp shared state: every tap's chunk offsets (loaded once), the tap's
+// bucket base and weight row, and the flattened-chunk prefix.
+struct WarpTabs {
+    int* off;          // [ntaps][OS]
+    int* pre;          // [32] first flattened position of each tap in this chunk
+    int* st;           // [32] bucket start of each tap in this chunk
+    long long* cbase;  // [32] column * C_in of each tap (-1: tap out of range)
+    int* wrow;         // [32] tap * C_in
+};
+
+__device__ __forceinline__ int tab_words(int ntaps, int OS) {
+    // off, pre, st, wrow as ints + cbase as 64-bit, padded to 16 B
+    return ((ntaps * OS + 3) & ~3) + 3 * 32 + 64;
+}
+
+template <int DELTA, int V, int EB, int MINB>
+__global__ void __launch_bounds__(WARPS * 32, MINB) k_integrate(IntegParams p, long long n_warps, int groups) {
+    extern __shared__ __align__(16) int smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* stage = smem + warp * (2 * EB * 32 * V);           // [2][EB][32][V]
-    int* s_pre = reinterpret_cast<int*>(smem + WARPS * 2 * EB * 32 * V) + warp * 64;
-    int* s_st = s_pre + 32;
-    float* s_decay = reinterpret_cast<float*>(reinterpret_cast<int*>(smem + WARPS * 2 * EB * 32 * V) + WARPS * 64);
+    const int ntaps = p.is_fc ? 1 : p.K * p.K;
+    const int OS = p.NC + 1;
+    const int words = tab_words(ntaps, OS);
+    WarpTabs tb;
+    tb.cbase = reinterpret_cast<long long*>(smem + warp * words);
+    tb.pre = smem + warp * words + 64;
+    tb.st = tb.pre + 32;
+    tb.wrow = tb.st + 32;
+    tb.off = tb.wrow + 32;
+    float* s_decay = reinterpret_cast<float*>(smem + WARPS * words);
     float* s_th = s_decay + p.decay_len;
+    float* s_min = s_th + p.T;                       // lowest firing threshold of each chunk
     for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
     for (int i = threadIdx.x; i < p.T; i += blockDim.x) s_th[i] = p.lut_th[i];
     __syncthreads();
+    for (int c = threadIdx.x; c < p.NC; c += blockDim.x) {
+        float mn = __int_as_float(0x7f800000);
+        for (int t = c * DELTA; t < min(p.T, (c + 1) * DELTA); ++t) {
+            const float th = s_th[t];
+            if (t >= p.t_min && th >= 1e-5f && th < mn) mn = th;
+        }
+        s_min[c] = mn;
+    }
+    __syncthreads();
 
     const long long gw = (long long)blockIdx.x * WARPS + warp;
-    if (gw >= n_warps) return;                                // warp-uniform
+    if (gw >= n_warps) return;                        // warp-uniform
     const long long pix = gw / groups;
     const int grp = (int)(gw - pix * groups);
     const int c0 = (grp * 32 + lane) * V;
@@ -195,21 +169,28 @@ __global__ void __launch_bounds__(WARPS * 32, 3) k_integrate(IntegParams p, long
         h_out = (int)(r % p.H_out);
         img = r / p.H_out;
     }
-    const int ntaps = p.is_fc ? 1 : p.K * p.K;
-    const int OS = p.NC + 1;
-
-    // lane j < ntaps owns tap j's input column (or none if out of range)
-    const int* my_off = nullptr;
+    // tap tables: lane j < ntaps describes tap j
     if (lane < ntaps) {
+        long long col = -1;
         if (p.is_fc) {
-            my_off = p.off + img * OS;
+            col = img;
         } else {
             const int kh = lane / p.K, kw = lane - (lane / p.K) * p.K;
             const int h_in = h_out - p.pad + kh, w_in = w_out - p.pad + kw;
             if (h_in >= 0 && h_in < p.H_in && w_in >= 0 && w_in < p.W_in)
-                my_off = p.off + ((img * p.H_in + h_in) * p.W_in + w_in) * OS;
+                col = (img * p.H_in + h_in) * p.W_in + w_in;
         }
+        tb.cbase[lane] = col < 0 ? -1 : col * p.C_in;
+        tb.wrow[lane] = p.is_fc ? 0 : lane * p.C_in;
     }
+    __syncwarp();
+    // every chunk offset of every tap, in one pass
+    for (int i = lane; i < ntaps * OS; i += 32) {
+        const int j = i / OS, c = i - j * OS;
+        const long long cb = tb.cbase[j];
+        tb.off[i] = cb < 0 ? 0 : __ldg(p.off + (cb / p.C_in) * OS + c);
+    }
+    __syncwarp();
 
     float carry[V], res[V];
     bool alive[V];
@@ -221,17 +202,19 @@ __global__ void __launch_bounds__(WARPS * 32, 3) k_integrate(IntegParams p, long
     }
     unsigned long long fetched = 0;
     const float* Wl = p.W + (lane_ok ? c0 : 0);
-
-    // chunk offsets one chunk ahead
-    int nx_s = 0, nx_e = 0;
-    if (my_off) { nx_s = __ldg(my_off); nx_e = __ldg(my_off + 1); }
+    float w[EB][V];
+#pragma unroll
+    for (int u = 0; u < EB; ++u)
+#pragma unroll
+        for (int v = 0; v < V; ++v) w[u][v] = 0.0f;
 
     for (int tau = 0; tau < p.NC; ++tau) {
         const int base = tau * DELTA;
-        const int my_s = nx_s, cnt = nx_e - nx_s;
-        if (my_off && tau + 1 < p.NC) { nx_s = __ldg(my_off + tau + 1); nx_e = __ldg(my_off + tau + 2); }
-
-        // flatten the taps' events of this chunk into one list, tap order kept
+        int cnt = 0, st = 0;
+        if (lane < ntaps) {
+            st = tb.off[lane * OS + tau];
+            cnt = tb.off[lane * OS + tau + 1] - st;
+        }
         int inc = cnt;
 #pragma unroll
         for (int dd = 1; dd < 32; dd <<= 1) {
@@ -239,62 +222,103 @@ __global__ void __launch_bounds__(WARPS * 32, 3) k_integrate(IntegParams p, long
             if (lane >= dd) inc += u;
         }
         const int total = __shfl_sync(FULL, inc, 31);
-        if (lane < ntaps) { s_pre[lane] = inc - cnt; s_st[lane] = my_s; }
-        __syncwarp();
-
-        float d[DELTA][V];
-#pragma unroll
-        for (int i = 0; i < DELTA; ++i)
-#pragma unroll
-            for (int v = 0; v < V; ++v) d[i][v] = 0.0f;
-
         int n_live = 0;
 #pragma unroll
         for (int v = 0; v < V; ++v) n_live += alive[v] ? 1 : 0;
-        const bool lane_live = n_live > 0;
         if (p.fetched) fetched += (unsigned long long)total * n_live;
 
-        if (total > 0) {
-            // batch pipeline: rows of batch b+1 are in flight while b is applied
-            Ev cur = load_event<DELTA>(p, lane < EB ? lane : total, total, s_pre, s_st, ntaps, img,
-                                       h_out, w_out, base, s_decay);
-            int ncur = min(EB, total);
-            stage_rows<V>(stage, cur, ncur, Wl, lane, lane_live);
-            int buf = 0;
-            for (int b0 = 0; b0 < total; b0 += EB) {
-                const int nb0 = b0 + EB;
-                Ev nxt{-1, 0, 0.0f};
-                int nnext = 0;
-                if (nb0 < total) {
-                    nnext = min(EB, total - nb0);
-                    nxt = load_event<DELTA>(p, lane < EB ? nb0 + lane : total, total, s_pre, s_st, ntaps,
-                                            img, h_out, w_out, base, s_decay);
-                    stage_rows<V>(stage + (buf ^ 1) * EB * 32 * V, nxt, nnext, Wl, lane, lane_live);
-                    cp_async_wait<1>();
-                } else {
-                    cp_async_wait<0>();
-                }
-                __syncwarp();
-                apply_batch<DELTA, V>(d, stage + buf * EB * 32 * V, cur, lane);
-                __syncwarp();
-                cur = nxt;
-                ncur = nnext;
-                buf ^= 1;
-            }
-        }
-        // integrate this chunk; first crossing wins (t1:150-157, t2:158-165)
+        if (total == 0) {
+            // no input in this chunk: the carry is constant, so a neuron fires
+            // in it iff the carry reaches the chunk's lowest firing threshold
+            const float mn = s_min[tau];
 #pragma unroll
-        for (int i = 0; i < DELTA; ++i) {
-            const int t = base + i;
-            if (t < p.T) {
-                const float th = s_th[t];
-#pragma unroll
-                for (int v = 0; v < V; ++v) {
-                    if (alive[v]) {
-                        carry[v] += d[i][v];
+            for (int v = 0; v < V; ++v) {
+                if (alive[v] && carry[v] >= mn) {
+                    for (int t = base; t < min(p.T, base + DELTA); ++t) {
+                        const float th = s_th[t];
                         if (t >= p.t_min && carry[v] >= th && th >= 1e-5f) {
                             res[v] = (float)t;
                             alive[v] = false;
+                            break;
+                        }
+                    }
+                }
+            }
+        } else {
+            if (lane < ntaps) { tb.pre[lane] = inc - cnt; tb.st[lane] = st; }
+            __syncwarp();
+            float d[DELTA][V];
+#pragma unroll
+            for (int i = 0; i < DELTA; ++i)
+#pragma unroll
+                for (int v = 0; v < V; ++v) d[i][v] = 0.0f;
+            const bool lane_live = n_live > 0;
+            for (int p0 = 0; p0 < total; p0 += 32) {
+                // decode event p0 + lane of the chunk's tap-ordered list
+                const int pidx = p0 + lane;
+                int slot = -1, wo = 0;
+                float lv = 0.0f;
+                if (pidx < total) {
+                    int lo = 0, hi = ntaps - 1;
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if (tb.pre[mid] <= pidx) lo = mid; else hi = mid - 1;
+                    }
+                    const long long at = tb.cbase[lo] + tb.st[lo] + (pidx - tb.pre[lo]);
+                    const int ci = __ldg(p.cin + at);
+                    const float t = __ldg(p.tin + at);
+                    int tbin = (int)floorf(t - p.tfs);
+                    if (tbin < 0) tbin = 0;
+                    int ti;
+                    if (p.lut_mode == VDT_LUT_BY_TB) {
+                        ti = tbin;
+                    } else {
+                        ti = (int)t;
+                        ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+                    }
+                    slot = tbin - base;
+                    lv = s_decay[ti];
+                    wo = (tb.wrow[lo] + ci) * p.C_out;
+                }
+                const int nb = min(32, total - p0);
+                int q0 = 0;
+                // full batches: EB weight rows in flight, then applied in order
+                for (; q0 + EB <= nb; q0 += EB) {
+#pragma unroll
+                    for (int u = 0; u < EB; ++u) {
+                        const int woq = __shfl_sync(FULL, wo, q0 + u);
+                        if (lane_live) load_vec<V>(Wl + woq, w[u]);
+                    }
+#pragma unroll
+                    for (int u = 0; u < EB; ++u) {
+                        const int sq = __shfl_sync(FULL, slot, q0 + u);
+                        const float lq = __shfl_sync(FULL, lv, q0 + u);
+                        add_event<DELTA, V>(d, sq, w[u], lq);
+                    }
+                }
+                for (; q0 < nb; ++q0) {
+                    const int woq = __shfl_sync(FULL, wo, q0);
+                    const int sq = __shfl_sync(FULL, slot, q0);
+                    const float lq = __shfl_sync(FULL, lv, q0);
+                    if (lane_live) load_vec<V>(Wl + woq, w[0]);
+                    add_event<DELTA, V>(d, sq, w[0], lq);
+                }
+            }
+            __syncwarp();
+            // integrate this chunk; first crossing wins (t1:150-157, t2:158-165)
+#pragma unroll
+            for (int i = 0; i < DELTA; ++i) {
+                const int t = base + i;
+                if (t < p.T) {
+                    const float th = s_th[t];
+#pragma unroll
+                    for (int v = 0; v < V; ++v) {
+                        if (alive[v]) {
+                            carry[v] += d[i][v];
+                            if (t >= p.t_min && carry[v] >= th && th >= 1e-5f) {
+                                res[v] = (float)t;
+                                alive[v] = false;
+                            }
                         }
                     }
                 }
@@ -314,24 +338,30 @@ __global__ void __launch_bounds__(WARPS * 32, 3) k_integrate(IntegParams p, long
 }
 
 // V (output channels per lane) for a layer: the widest of 4/2/1 that divides
-// C_out and keeps the per-lane delta[DELTA][V] block at <= 64 registers.
+// C_out and keeps the per-lane delta[DELTA][V] block at <= 32 registers.
 int pick_v(int C_out, int delta) {
-    if (C_out % 4 == 0 && C_out >= 128 && delta * 4 <= 64) return 4;
-    if (C_out % 2 == 0 && C_out >= 64 && delta * 2 <= 64) return 2;
+    if (C_out % 4 == 0 && C_out >= 128 && delta * 4 <= 32) return 4;
+    if (C_out % 2 == 0 && C_out >= 64 && delta * 2 <= 32) return 2;
     return 1;
 }
 
 template <int DELTA, int V>
 cudaError_t launch_dv(const IntegParams& p, cudaStream_t s, long long n_warps, int groups) {
     const long long blocks = (n_warps + WARPS - 1) / WARPS;
-    const size_t smem = (size_t)WARPS * 2 * EB * 32 * V * sizeof(float) + WARPS * 64 * sizeof(int) +
-                        (size_t)(p.decay_len + p.T) * sizeof(float);
+    const int ntaps = p.is_fc ? 1 : p.K * p.K;
+    const int OS = p.NC + 1;
+    const int words = ((ntaps * OS + 3) & ~3) + 3 * 32 + 64;
+    const size_t smem = (size_t)WARPS * words * sizeof(int) + (size_t)(p.decay_len + p.T + p.NC) * sizeof(float);
+    // resident CTAs per SM, from a register estimate: delta block + weight
+    // batch + ~48 for the rest (ptxas then fits the kernel without spills)
+    constexpr int REGS = DELTA * V + 4 * V + 48;
+    constexpr int MINB = (65536 / (WARPS * 32 * REGS)) > 8 ? 8 : (65536 / (WARPS * 32 * REGS));
+    auto kern = k_integrate<DELTA, V, 4, MINB>;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(k_integrate<DELTA, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    k_integrate<DELTA, V><<<(unsigned)blocks, WARPS * 32, smem, s>>>(p, n_warps, groups);
+    kern<<<(unsigned)blocks, WARPS * 32, smem, s>>>(p, n_warps, groups);
     return cudaGetLastError();
 }
 
@@ -343,8 +373,8 @@ cudaError_t launch_delta(const IntegParams& p, cudaStream_t s) {
     const long long n_warps = pixels * groups;
     if (n_warps <= 0) return cudaSuccess;
     switch (V) {
-        case 4: return launch_dv<DELTA, (DELTA <= 16 ? 4 : 1)>(p, s, n_warps, groups);
-        case 2: return launch_dv<DELTA, (DELTA <= 32 ? 2 : 1)>(p, s, n_warps, groups);
+        case 4: return launch_dv<DELTA, (DELTA <= 8 ? 4 : 1)>(p, s, n_warps, groups);
+        case 2: return launch_dv<DELTA, (DELTA <= 16 ? 2 : 1)>(p, s, n_warps, groups);
         default: return launch_dv<DELTA, 1>(p, s, n_warps, groups);
     }
 }
@@ -355,7 +385,9 @@ bool integrate_supported(int K, int is_fc, int delta, int C_out, int T, int deca
     if (!is_fc && (K < 1 || K * K > 32)) return false;
     if (delta != 1 && delta != 2 && delta != 4 && delta != 8 && delta != 16 && delta != 32 && delta != 64)
         return false;
-    if ((size_t)(decay_len + T) * sizeof(float) > 64 * 1024) return false;
+    const int OS = (T + delta - 1) / delta + 1, ntaps = is_fc ? 1 : K * K;
+    if ((size_t)WARPS * (((ntaps * OS + 3) & ~3) + 160) * 4 + (size_t)(decay_len + T + OS) * 4 > 200 * 1024)
+        return false;
     return C_out > 0;
 }
 

@@ -149,6 +149,7 @@ struct vdt_ctx {
     bool graphs = true;
     bool counting = false;
     bool profiling = false;
+    bool stream_integrator = false;  // time-sorted buckets + k_stream instead of k_integrate
     std::map<GraphKey, cudaGraphExec_t> cache;
     // profiling: (layer, stage, start, stop) per timed launch, read back lazily
     struct Mark { int layer, stage; cudaEvent_t a, b; };
@@ -389,7 +390,8 @@ struct Sizes {
 
 Sizes ctx_sizes(const vdt_model* m, long long B) {
     Sizes s;
-    const int OS = (m->cfg.T + m->cfg.delta - 1) / m->cfg.delta + 1;
+    // room for fine (delta = 1) offsets, the larger of the two bucket layouts
+    const int OS = std::max((m->cfg.T + m->cfg.delta - 1) / m->cfg.delta + 1, m->cfg.T + 1);
     s.act = (size_t)B * m->net.in_h * m->net.in_w * m->net.in_c;
     for (auto& ly : m->layers) {
         const size_t in = (size_t)B * ly.H_in * ly.W_in * ly.C_in;
@@ -447,13 +449,19 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
                                        cfg.fire_start, cfg.inf_time, y, s));
         } else {
             const bool fc = ly.d.kind == VDT_FC;
+            // time-sorted (delta = 1) buckets feed the stream integrator;
+            // chunk-granular ones the reference-layout integrator
+            const bool fine = c->stream_integrator &&
+                              stream_supported(fc ? 1 : ly.d.k, fc, cfg.delta, cfg.T, cfg.decay_len);
             BktParams bp{};
             bp.in = x;
             bp.n_cols = fc ? B : (long long)B * ly.H_in * ly.W_in;
             bp.c_in = ly.C_in;
             bp.layout = VDT_LAYOUT_NHWC;
             bp.hw = 1;
-            bp.T = cfg.T; bp.delta = cfg.delta; bp.NC = NC;
+            bp.T = cfg.T;
+            bp.delta = fine ? 1 : cfg.delta;
+            bp.NC = fine ? cfg.T : NC;
             bp.tfs = cfg.fire_start;
             bp.tb_mode = VDT_TB_FLOOR_STAGGER;
             bp.inf_time = cfg.inf_time;
@@ -477,7 +485,8 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
             ip.tfs = cfg.fire_start; ip.inf_time = cfg.inf_time;
             ip.fetched = fe;
             StageTimer st(c, i, 1);
-            VDT_CUDA(launch_integrate(ip, s));
+            if (fine) VDT_CUDA(launch_stream(ip, c->off, s));
+            else VDT_CUDA(launch_integrate(ip, s));
         }
         if (trace && trace[i] && y != trace[i])
             VDT_CUDA(cudaMemcpyAsync(trace[i], y, (size_t)B * ly.H_out * ly.W_out * ly.C_out * sizeof(float),

@@ -46,6 +46,11 @@ cudaError_t launch_integrate(const IntegParams& p, cudaStream_t s);
 // true when launch_integrate supports this (K, delta, C_out) combination
 bool integrate_supported(int K, int is_fc, int delta, int C_out, int T, int decay_len);
 
+// Fused-path integrator over buckets sorted at delta = 1 (fine offsets
+// foff[col * (T + 1) + tb]); same results as launch_integrate.
+cudaError_t launch_stream(const IntegParams& p, const int* foff, cudaStream_t s);
+bool stream_supported(int K, int is_fc, int delta, int T, int decay_len);
+
 // -------------------------------------------------------------- edges / LUT
 struct LutJob {            // one layer's table pair
     float tc_integ, td_integ, tc_fire, td_fire;
