@@ -78,6 +78,30 @@ __device__ __forceinline__ void add_case(float (&d)[DELTA][V], const float (&w)[
     for (int v = 0; v < V; ++v) d[S][v] = fmaf(w[v], lv, d[S][v]);
 }
 
+// EB events of one slot, applied in order: one dispatch for the whole batch.
+template <int DELTA, int V, int EB, int S>
+__device__ __forceinline__ void add_case_n(float (&d)[DELTA][V], const float (&w)[EB][V], const float (&lv)[EB]) {
+#pragma unroll
+    for (int u = 0; u < EB; ++u)
+#pragma unroll
+        for (int v = 0; v < V; ++v) d[S][v] = fmaf(w[u][v], lv[u], d[S][v]);
+}
+
+template <int DELTA, int V, int EB>
+__device__ __forceinline__ void add_events_same(float (&d)[DELTA][V], int slot, const float (&w)[EB][V],
+                                                const float (&lv)[EB]) {
+#define VDT_N(S) case S: if constexpr (S < DELTA) add_case_n<DELTA, V, EB, S>(d, w, lv); break;
+    if constexpr (DELTA <= 8) {
+        switch (slot) { VDT_N(0) VDT_N(1) VDT_N(2) VDT_N(3) VDT_N(4) VDT_N(5) VDT_N(6) VDT_N(7) default: break; }
+    } else {
+        switch (slot) {
+            VDT_N(0) VDT_N(1) VDT_N(2) VDT_N(3) VDT_N(4) VDT_N(5) VDT_N(6) VDT_N(7)
+            VDT_N(8) VDT_N(9) VDT_N(10) VDT_N(11) VDT_N(12) VDT_N(13) VDT_N(14) VDT_N(15) default: break;
+        }
+    }
+#undef VDT_N
+}
+
 template <int DELTA, int V>
 __device__ __forceinline__ void add_event(float (&d)[DELTA][V], int slot, const float (&w)[V], float lv) {
 #define VDT_C(S) case S: if constexpr (S < DELTA) add_case<DELTA, V, S>(d, w, lv); break;
@@ -289,11 +313,22 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) k_integrate(IntegParams p, l
                         const int woq = __shfl_sync(FULL, wo, q0 + u);
                         if (lane_live) load_vec<V>(Wl + woq, w[u]);
                     }
+                    float lq[EB];
 #pragma unroll
-                    for (int u = 0; u < EB; ++u) {
-                        const int sq = __shfl_sync(FULL, slot, q0 + u);
-                        const float lq = __shfl_sync(FULL, lv, q0 + u);
-                        add_event<DELTA, V>(d, sq, w[u], lq);
+                    for (int u = 0; u < EB; ++u) lq[u] = __shfl_sync(FULL, lv, q0 + u);
+                    const int s0 = __shfl_sync(FULL, slot, q0);
+                    const unsigned bm = ((1u << EB) - 1u) << q0;
+                    bool one_slot = false;
+                    if constexpr (DELTA <= 16) one_slot = (__ballot_sync(FULL, slot == s0) & bm) == bm;
+                    if (one_slot) {
+                        // the whole batch is in one slot (the common case): one dispatch
+                        if constexpr (DELTA <= 16) add_events_same<DELTA, V, EB>(d, s0, w, lq);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < EB; ++u) {
+                            const int sq = __shfl_sync(FULL, slot, q0 + u);
+                            add_event<DELTA, V>(d, sq, w[u], lq[u]);
+                        }
                     }
                 }
                 for (; q0 < nb; ++q0) {

@@ -149,7 +149,7 @@ struct vdt_ctx {
     bool graphs = true;
     bool counting = false;
     bool profiling = false;
-    bool stream_integrator = false;  // time-sorted buckets + k_stream instead of k_integrate
+    int dense_max_fan = 1152;        // layers with K*K*C_in up to this use k_dense
     std::map<GraphKey, cudaGraphExec_t> cache;
     // profiling: (layer, stage, start, stop) per timed launch, read back lazily
     struct Mark { int layer, stage; cudaEvent_t a, b; };
@@ -390,8 +390,7 @@ struct Sizes {
 
 Sizes ctx_sizes(const vdt_model* m, long long B) {
     Sizes s;
-    // room for fine (delta = 1) offsets, the larger of the two bucket layouts
-    const int OS = std::max((m->cfg.T + m->cfg.delta - 1) / m->cfg.delta + 1, m->cfg.T + 1);
+    const int OS = (m->cfg.T + m->cfg.delta - 1) / m->cfg.delta + 1;
     s.act = (size_t)B * m->net.in_h * m->net.in_w * m->net.in_c;
     for (auto& ly : m->layers) {
         const size_t in = (size_t)B * ly.H_in * ly.W_in * ly.C_in;
@@ -449,28 +448,8 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
                                        cfg.fire_start, cfg.inf_time, y, s));
         } else {
             const bool fc = ly.d.kind == VDT_FC;
-            // time-sorted (delta = 1) buckets feed the stream integrator;
-            // chunk-granular ones the reference-layout integrator
-            const bool fine = c->stream_integrator &&
-                              stream_supported(fc ? 1 : ly.d.k, fc, cfg.delta, cfg.T, cfg.decay_len);
-            BktParams bp{};
-            bp.in = x;
-            bp.n_cols = fc ? B : (long long)B * ly.H_in * ly.W_in;
-            bp.c_in = ly.C_in;
-            bp.layout = VDT_LAYOUT_NHWC;
-            bp.hw = 1;
-            bp.T = cfg.T;
-            bp.delta = fine ? 1 : cfg.delta;
-            bp.NC = fine ? cfg.T : NC;
-            bp.tfs = cfg.fire_start;
-            bp.tb_mode = VDT_TB_FLOOR_STAGGER;
-            bp.inf_time = cfg.inf_time;
-            bp.off = c->off; bp.cin = c->cin; bp.tin = c->tin;
-            bp.events = ev;
-            {
-                StageTimer st(c, i, 0);
-                VDT_CUDA(launch_bucketize(bp, s));
-            }
+            // small fan-in: the integrator reads the spike map itself (no
+            // bucket pass); otherwise bucketize, then integrate
             IntegParams ip{};
             ip.off = c->off; ip.cin = c->cin; ip.tin = c->tin;
             ip.W = ly.W; ip.bias = ly.bias; ip.lut_decay = ly.decay; ip.lut_th = ly.th;
@@ -484,8 +463,32 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
             ip.lut_mode = cfg.lut_mode; ip.decay_len = cfg.decay_len;
             ip.tfs = cfg.fire_start; ip.inf_time = cfg.inf_time;
             ip.fetched = fe;
+            const int fan = (fc ? 1 : ly.d.k * ly.d.k) * ly.C_in;
+            const bool dense = fan <= c->dense_max_fan &&
+                               dense_supported(ly.d.k, fc, ly.C_in, cfg.T, cfg.decay_len);
+            if (!dense || ev) {
+                // the dense path needs no buckets; they are still built when
+                // counting, for the event counter
+                BktParams bp{};
+                bp.in = x;
+                bp.n_cols = fc ? B : (long long)B * ly.H_in * ly.W_in;
+                bp.c_in = ly.C_in;
+                bp.layout = VDT_LAYOUT_NHWC;
+                bp.hw = 1;
+                bp.T = cfg.T;
+                bp.delta = cfg.delta;
+                bp.NC = NC;
+                bp.tfs = cfg.fire_start;
+                bp.tb_mode = VDT_TB_FLOOR_STAGGER;
+                bp.inf_time = cfg.inf_time;
+                bp.off = c->off; bp.cin = c->cin; bp.tin = c->tin;
+                bp.events = ev;
+                StageTimer st(c, i, 0);
+                VDT_CUDA(launch_bucketize(bp, s));
+            }
             StageTimer st(c, i, 1);
-            if (fine) VDT_CUDA(launch_stream(ip, c->off, s));
+            if (dense) VDT_CUDA(launch_dense(ip, x, s));
+            else if (sorted_supported(ip.K, fc, cfg.delta, ly.C_in, cfg.T, cfg.decay_len)) VDT_CUDA(launch_sorted(ip, s));
             else VDT_CUDA(launch_integrate(ip, s));
         }
         if (trace && trace[i] && y != trace[i])

@@ -46,10 +46,15 @@ cudaError_t launch_integrate(const IntegParams& p, cudaStream_t s);
 // true when launch_integrate supports this (K, delta, C_out) combination
 bool integrate_supported(int K, int is_fc, int delta, int C_out, int T, int decay_len);
 
-// Fused-path integrator over buckets sorted at delta = 1 (fine offsets
-// foff[col * (T + 1) + tb]); same results as launch_integrate.
-cudaError_t launch_stream(const IntegParams& p, const int* foff, cudaStream_t s);
-bool stream_supported(int K, int is_fc, int delta, int T, int decay_len);
+// Integrator fused with the bucketing for small per-pixel fan-in: reads the
+// NHWC spike map `in` directly (same results as bucketize + integrate).
+cudaError_t launch_dense(const IntegParams& p, const float* in, cudaStream_t s);
+bool dense_supported(int K, int is_fc, int C_in, int T, int decay_len);
+
+// Chunk integrator with per-chunk slot sorting (reference bucket layout,
+// same results as launch_integrate, fewer instructions per event).
+cudaError_t launch_sorted(const IntegParams& p, cudaStream_t s);
+bool sorted_supported(int K, int is_fc, int delta, int C_in, int T, int decay_len);
 
 // -------------------------------------------------------------- edges / LUT
 struct LutJob {            // one layer's table pair
