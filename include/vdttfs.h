@@ -202,6 +202,34 @@ int vdt_pool_min(const float* d_in, float* d_out, int B, int H_in, int W_in, int
 int vdt_readout(const float* d_out, int B, int K, int mode, float inf_time,
                 int32_t* d_pred, vdt_stream stream);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free layer step (no counterpart in the reference)
+ * ---------------------------------------------------------------------- */
+
+/* Bytes of the library's fixed per-device scratch array. */
+#define VDT_NOALLOC_SCRATCH_BYTES (32u << 20)
+size_t vdt_noalloc_scratch_bytes(void);
+
+/* One fire layer -- vdt_bucketize (NHWC, tb_mode) followed by
+   vdt_conv_bucketed, same arguments and same results -- for callers that
+   cannot let a library allocate device memory while they run (servers that
+   plan all device memory up front, loops that cannot take cudaMalloc's
+   device-wide synchronisation, hosts that own the allocator).  It allocates
+   nothing: the bucket lists live in a static device array of
+   VDT_NOALLOC_SCRATCH_BYTES per GPU.  A layer whose lists need more
+   (n_cols*(NC+1) + 2*n_cols*C_in 4-byte words, each of the three parts rounded
+   up to 256 bytes; n_cols = B*H_in*W_in, or B for is_fc) returns
+   VDT_ERR_CAPACITY and launches nothing.  The first call on each device looks
+   the array's address up (with that device current) and should precede any
+   stream capture.  Calls on one device share the array, so calls that can
+   overlap on the GPU (unordered streams or threads) race; order them.
+   Nothing in the array needs to start zeroed. */
+int vdt_conv_layer_noalloc(const float* d_in, int tb_mode, const float* d_kernel,
+                           const float* d_bias, const float* d_decay, const float* d_th,
+                           int t_min, int B, int H_in, int W_in, int C_in, int H_out,
+                           int W_out, int C_out, int K, int pad, int is_fc,
+                           const vdt_time_cfg* cfg, float* d_out, vdt_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -85,6 +85,17 @@ int check_cfg(const vdt_time_cfg* c) {
     return VDT_OK;
 }
 
+}  // namespace
+
+namespace vdt {
+void api_clear_error() { g_last_error.clear(); }
+int api_fail(int status, const char* msg) { return fail(status, "%s", msg); }
+int api_cuda_fail(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+int api_check_cfg(const vdt_time_cfg* c) { return check_cfg(c); }
+}  // namespace vdt
+
+namespace {
+
 struct Layer {
     vdt_layer_desc d;
     int H_in, W_in, C_in, H_out, W_out, C_out;

@@ -9,6 +9,12 @@
 
 namespace vdt {
 
+// error reporting shared by every C entry point (vdt_last_error)
+void api_clear_error();
+int api_fail(int status, const char* msg);
+int api_cuda_fail(cudaError_t e, const char* what);
+int api_check_cfg(const vdt_time_cfg* c);
+
 // ---------------------------------------------------------------- bucketize
 struct BktParams {
     const float* in;
