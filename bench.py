@@ -11,10 +11,11 @@ int32 predictions when N > 1.
           runs between steps, outside the timed events.
   e2e     the same through vdt_infer_host: pinned host pixels -> H2D -> the
           network -> D2H of the logits and predictions, every step.
-  roofline  the integrator (k_integrate, all launches of a step) timed live
-          with CUDA events around each launch (eager profiling pass), against
-          its algorithmic bytes: events read (8 B each), chunk offsets read,
-          first-spike map written, weights read once per launch.
+  roofline  the bucketize + integrator launches of a step (k_bucketize,
+          k_dense, k_sorted, k_integrate, k_layer_vmem), timed live with CUDA
+          events around each launch (eager profiling pass), against their
+          implementation-independent algorithmic bytes (layer_bytes); traffic
+          is the DRAM bytes ncu measured for the same launches.
   cpu_baseline  the CPU oracle port (OpenMP over all host cores) on a bounded
           sample of the same workload.
 
@@ -52,6 +53,8 @@ def parse():
     ap.add_argument("--config", default="vgg16", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the config's batch (small cases for profiling; not a bench line)")
     return ap.parse_args()
 
 
@@ -123,29 +126,33 @@ def peaks():
 
 
 # ------------------------------------------------------------- algorithmic --
-def integrator_bytes(net, events_per_layer, B):
-    """Algorithmic bytes of every k_integrate launch of one step (and of the
-    membrane readout on the last layer): 8 B per event read (cin + t_in),
-    4 B per chunk offset read, 4 B per output neuron written, the layer's
-    weights read once."""
+def layer_bytes(net, events_per_layer, B):
+    """Algorithmic bytes of the bucketize + integrate work of each layer for a
+    batch of B, implementation-independent: read the input spike map (4 B per
+    value), write the first-spike map (4 B per neuron), write and read back
+    the bucket lists (8 B per kept event: channel + time) and chunk offsets
+    (4 B per column per offset), read the weights once per batch.  The
+    membrane-readout layer has no bucket lists."""
     OS = net.n_chunks + 1
-    total = 0
+    per = []
     for (l, shp, E) in zip(net.layers, net.shapes(), events_per_layer):
         H_in, W_in, C_in, H_out, W_out, C_out = shp
+        n_in = B * H_in * W_in * C_in
         n_out = B * H_out * W_out * C_out
         wts = (l.k * l.k if l.kind == 0 else 1) * C_in * C_out
-        if l.out == 1:       # membrane readout reads the dense input map
-            total += 4 * B * C_in + 4 * n_out + 4 * wts
-            continue
         cols = B if l.kind == 1 else B * H_in * W_in
-        total += 8 * E + 4 * cols * OS + 4 * n_out + 4 * wts
-    return total
+        lists = 0 if l.out == 1 else 2 * (8 * E + 4 * cols * OS)
+        per.append(4 * n_in + 4 * n_out + lists + 4 * wts)
+    return per
 
 
-def launches_per_step(net, pixels=True):
+def launches_per_step(net, kernels, pixels=True):
+    """Kernel launches of one inference: encode, per layer bucketize (not for
+    k_dense / k_layer_vmem layers) + integrator, pools, readout."""
+    from vdttfs.engine import KERNEL_DENSE, KERNEL_VMEM
     n = 1 if pixels else 0
-    for l in net.layers:
-        n += 1 if l.out == 1 else 2
+    for l, k in zip(net.layers, kernels):
+        n += 1 if k in (KERNEL_DENSE, KERNEL_VMEM) else 2
         n += 1 if l.pool_after else 0
     return n + 1        # readout
 
@@ -167,6 +174,8 @@ def run_engine(a):
 
     netname, cfg_id, Bcfg, zf, scaling = CONFIGS[a.config]
     net = nets.NETS[netname]()
+    if a.batch:
+        Bcfg = a.batch
     B = Bcfg // world if scaling == "strong" else Bcfg
     layers = synth.kaiming_layers(net, cfg_id)
     img = synth.images(cfg_id, B, net.in_h, net.in_w, net.in_c, zf, stream=rank)
@@ -259,12 +268,14 @@ def run_engine(a):
             ctx.infer(x_dev, pixels=True, out=out, pred=pred)
     bkt_ms, int_ms, pool_ms, nb = ctx.layer_times()
     ctx.set_profiling(False)
-    # events per layer from the oracle-independent bucket counts: re-run with counting per layer
+    kernels = ctx.layer_kernels()
+    # kept events per layer, from the engine's own bucket offsets
     per_layer_events = layer_events(E, net, layers, x_dev, B, dev)
-    int_bytes = integrator_bytes(net, per_layer_events, B)
-    int_step_ms = float(np.sum(int_ms)) / nb
+    lbytes = layer_bytes(net, per_layer_events, B)
+    alg_bytes = int(sum(lbytes))
+    work_ms = (float(np.sum(bkt_ms)) + float(np.sum(int_ms))) / nb
     peak, peak_kind = peaks()
-    achieved = int_bytes / (int_step_ms / 1e3) / 1e9
+    achieved = alg_bytes / (work_ms / 1e3) / 1e9
 
     if world > 1:
         dist.barrier()
@@ -283,14 +294,18 @@ def run_engine(a):
                     "h2d_bytes_per_step": int(img.nbytes),
                     "d2h_bytes_per_step": int(B * net.n_classes * 4 + B * 4)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
-                         "kernel": "k_integrate (all launches of a step)",
-                         "peak_source": peak_kind,
-                         "algorithmic_bytes_per_step": int(int_bytes),
-                         "integrate_ms_per_step": round(int_step_ms, 4),
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic_per_step(netname, B),
+                         "kernel": "bucketize + integrators, all launches of one step ("
+                                   + ", ".join(f"L{i}:{E.KERNEL_NAMES[k]}" for i, k in enumerate(kernels)) + ")",
+                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "algorithmic_bytes_per_step": alg_bytes,
+                         "algorithmic_bytes_per_layer": [int(v) for v in lbytes],
+                         "kernel_ms_per_step": round(work_ms, 4),
+                         "integrate_ms_per_layer": [round(float(v) / nb, 4) for v in int_ms],
                          "bucketize_ms_per_step": round(float(np.sum(bkt_ms)) / nb, 4),
                          "pool_ms_per_step": round(float(np.sum(pool_ms)) / nb, 4)},
-            "gpu_launches": launches_per_step(net) * a.steps,
+            "gpu_launches": launches_per_step(net, kernels) * a.steps,
             "events_per_image": round(ev_total / B, 1),
             "fetched_synapses_per_image": round(fetched / B, 1),
             "clocks": clk,
@@ -301,6 +316,17 @@ def run_engine(a):
         del ctx
         dist.destroy_process_group()
     return res
+
+
+# DRAM bytes (read + write) per image of the bucketize + integrator launches,
+# from ncu's dram__bytes_read.sum + dram__bytes_write.sum over one step
+# (summary and command in profiles/traffic_vgg16_b256.md).
+DRAM_BYTES_PER_IMAGE = {"vgg16": 1299912}
+
+
+def traffic_per_step(netname, B):
+    v = DRAM_BYTES_PER_IMAGE.get(netname)
+    return None if v is None else int(round(v * B))
 
 
 def layer_events(E, net, layers, x_dev, B, dev):

@@ -134,6 +134,17 @@ int vdt_ctx_set_profiling(vdt_ctx* c, int enable);
 int vdt_ctx_layer_times(vdt_ctx* c, int n_layers, float* bucketize_ms, float* integrate_ms,
                         float* pool_ms, int* batches);
 
+/* Integrator each layer runs (no counterpart in the reference, which has one
+   kernel).  A layer with VDT_KERNEL_DENSE launches no bucketize pass unless
+   counting is on. */
+enum {
+    VDT_KERNEL_CHUNK = 0,   /* k_integrate: chunk-bucket integrator (t2:84-170 order) */
+    VDT_KERNEL_SORTED = 1,  /* k_sorted: per-chunk slot-sorted buckets, same results */
+    VDT_KERNEL_DENSE = 2,   /* k_dense: bucketing fused, reads the spike map */
+    VDT_KERNEL_VMEM = 3     /* k_layer_vmem membrane readout */
+};
+int vdt_ctx_layer_kernels(const vdt_ctx* c, int n_layers, int* kernels);
+
 /* ------------------------------------------------------------------------
  * Whole-network inference: the per-batch body of the reference's main
  * (t1:290-315, t2:341-392).  d_input is [batch, in_h, in_w, in_c]: spike

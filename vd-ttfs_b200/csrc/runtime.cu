@@ -170,6 +170,19 @@ struct vdt_ctx {
 };
 
 namespace {
+// which integrator runs a layer: k_dense (bucketing fused in) for small
+// per-pixel fan-in, else k_sorted, else the generic chunk integrator
+int layer_kernel(const vdt_ctx* c, const Layer& ly, const vdt_time_cfg& cfg) {
+    if (ly.d.out == VDT_OUT_VMEM) return VDT_KERNEL_VMEM;
+    const int fc = ly.d.kind == VDT_FC;
+    const int K = fc ? 1 : ly.d.k;
+    const int fan = K * K * ly.C_in;
+    if (fan <= c->dense_max_fan && dense_supported(ly.d.k, fc, ly.C_in, cfg.T, cfg.decay_len))
+        return VDT_KERNEL_DENSE;
+    if (sorted_supported(K, fc, cfg.delta, ly.C_in, cfg.T, cfg.decay_len)) return VDT_KERNEL_SORTED;
+    return VDT_KERNEL_CHUNK;
+}
+
 cudaEvent_t take_event(vdt_ctx* c) {
     if (!c->spare_events.empty()) {
         cudaEvent_t e = c->spare_events.back();
@@ -474,9 +487,8 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
             ip.lut_mode = cfg.lut_mode; ip.decay_len = cfg.decay_len;
             ip.tfs = cfg.fire_start; ip.inf_time = cfg.inf_time;
             ip.fetched = fe;
-            const int fan = (fc ? 1 : ly.d.k * ly.d.k) * ly.C_in;
-            const bool dense = fan <= c->dense_max_fan &&
-                               dense_supported(ly.d.k, fc, ly.C_in, cfg.T, cfg.decay_len);
+            const int kern = layer_kernel(c, ly, cfg);
+            const bool dense = kern == VDT_KERNEL_DENSE;
             if (!dense || ev) {
                 // the dense path needs no buckets; they are still built when
                 // counting, for the event counter
@@ -499,7 +511,7 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
             }
             StageTimer st(c, i, 1);
             if (dense) VDT_CUDA(launch_dense(ip, x, s));
-            else if (sorted_supported(ip.K, fc, cfg.delta, ly.C_in, cfg.T, cfg.decay_len)) VDT_CUDA(launch_sorted(ip, s));
+            else if (kern == VDT_KERNEL_SORTED) VDT_CUDA(launch_sorted(ip, s));
             else VDT_CUDA(launch_integrate(ip, s));
         }
         if (trace && trace[i] && y != trace[i])
@@ -611,6 +623,14 @@ extern "C" int vdt_ctx_layer_times(vdt_ctx* c, int n_layers, float* bkt_ms, floa
     c->marks.clear();
     if (batches) *batches = c->prof_batches;
     c->prof_batches = 0;
+    return VDT_OK;
+}
+
+extern "C" int vdt_ctx_layer_kernels(const vdt_ctx* c, int n_layers, int* kernels) {
+    g_last_error.clear();
+    if (!c || !kernels) return fail(VDT_ERR_INVALID, "ctx or kernels is NULL");
+    if (n_layers != (int)c->m->layers.size()) return fail(VDT_ERR_INVALID, "n_layers mismatch");
+    for (int i = 0; i < n_layers; ++i) kernels[i] = layer_kernel(c, c->m->layers[i], c->m->cfg);
     return VDT_OK;
 }
 

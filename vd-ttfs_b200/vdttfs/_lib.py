@@ -72,6 +72,7 @@ SIGNATURES = {
                                  C.POINTER(TimeCfg), _vp, _vp]),
     "vdt_pool_min": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _vp]),
     "vdt_readout": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_float, _vp, _vp]),
+    "vdt_ctx_layer_kernels": (C.c_int, [_vp, C.c_int, _vp]),
     "vdt_noalloc_scratch_bytes": (C.c_size_t, []),
     "vdt_conv_layer_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, C.c_int, C.c_int,
                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
