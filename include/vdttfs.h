@@ -144,6 +144,10 @@ enum {
     VDT_KERNEL_VMEM = 3     /* k_layer_vmem membrane readout */
 };
 int vdt_ctx_layer_kernels(const vdt_ctx* c, int n_layers, int* kernels);
+/* Force the integrator of one layer (-1 = automatic choice); results are the
+   same with every kernel, only speed differs.  VDT_ERR_UNSUPPORTED if that
+   kernel cannot run the layer.  Drops the ctx's captured graphs. */
+int vdt_ctx_set_layer_kernel(vdt_ctx* c, int layer, int kernel);
 
 /* ------------------------------------------------------------------------
  * Whole-network inference: the per-batch body of the reference's main

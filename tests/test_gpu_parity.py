@@ -262,6 +262,47 @@ def test_network_bitexact_host_luts(O, dev, name, B, cfg_id, zero_frac):
     assert bits_equal(_np(out2), ref["out"]) and np.array_equal(_np(pred2), ref["pred"])
 
 
+@pytest.mark.parametrize("kernel", [0, 1, 2])
+def test_every_integrator_choice_is_bitexact(O, dev, kernel):
+    """Forcing k_integrate / k_sorted / k_dense on every layer that kernel
+    supports changes nothing: maps, outputs and counters stay bit-identical
+    to the oracle (graph path and eager path)."""
+    from vdttfs import engine as E
+    net, layers, img = _net_case("vgg16", 5, 3, 0.0)
+    spikes = O.encode_linear(img, net.T)
+    ref = O.run_net(net, layers, spikes, keep=True)
+    m = E.Model(net, layers, lut_source=E.LUT_HOST_LIBM)
+    ctx = E.Context(m, 5)
+    forced = 0
+    for li in range(len(net.layers)):
+        try:
+            ctx.set_layer_kernel(li, kernel)
+            forced += 1
+        except E.VdtError as e:
+            assert e.status == 5                      # VDT_ERR_UNSUPPORTED
+    assert forced >= 3
+    kinds = ctx.layer_kernels()
+    assert sum(k == kernel for k in kinds) == forced
+    ctx.set_counting(True)
+    maps, out, pred = ctx.trace(_t(spikes, dev))
+    _sync()
+    events, fetched = ctx.counters()
+    ri = 0
+    for li, l in enumerate(net.layers):
+        assert bits_equal(_np(maps[li]).reshape(-1), ref["maps"][ri]), f"layer {li} differs"
+        ri += 2 if l.pool_after else 1
+    assert bits_equal(_np(out), ref["out"]) and np.array_equal(_np(pred), ref["pred"])
+    assert events == sum(ref["events"]) and fetched == sum(ref["fetched"])
+    ctx.set_counting(False)
+    out2, pred2 = ctx.infer(_t(spikes, dev))
+    _sync()
+    assert bits_equal(_np(out2), ref["out"])
+    with pytest.raises(E.VdtError):
+        ctx.set_layer_kernel(len(net.layers) - 1, 0)  # membrane-readout layer
+    with pytest.raises(E.VdtError):
+        ctx.set_layer_kernel(0, 9)
+
+
 def test_network_device_luts_tolerance(O, dev):
     """Device-built LUTs (<= 1 ulp from libm): layer by layer on identical
     inputs, any spike-time difference must come from a neuron whose membrane

@@ -99,8 +99,15 @@ struct DLane {
 #pragma unroll
             for (int v = 0; v < V; ++v) {
                 if (alive[v] && carry[v] >= mn) {
-                    for (int t = lo; t < hi; ++t)
-                        if (carry[v] >= s_th[t]) { res[v] = (float)t; alive[v] = false; break; }
+                    // thresholds are non-increasing: the first step whose
+                    // threshold the constant carry reaches, by bisection
+                    int l = lo, h = hi - 1;
+                    while (l < h) {
+                        const int mid = (l + h) >> 1;
+                        if (carry[v] >= s_th[mid]) h = mid; else l = mid + 1;
+                    }
+                    res[v] = (float)l;
+                    alive[v] = false;
                 }
             }
         } else {
@@ -128,7 +135,7 @@ __device__ __forceinline__ int tap_of(int f, int C_in, float inv) {
 
 template <int V, int R, int MINB>
 __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const float* __restrict__ in,
-                                                         long long n_warps, int groups) {
+                                                         int n_warps, int groups) {
     extern __shared__ __align__(16) int sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
@@ -153,19 +160,20 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
     const bool monotone = s_mono != 0;
     const int t_floor = s_floor;
 
-    const long long gw = (long long)blockIdx.x * DW + warp;
+    const int gw = blockIdx.x * DW + warp;
     if (gw >= n_warps) return;                               // warp-uniform
-    const long long pix = gw / groups;
-    const int grp = (int)(gw - pix * groups);
+    const unsigned pix = (unsigned)gw / (unsigned)groups;
+    const int grp = gw - (int)pix * groups;
     const int c0 = (grp * 32 + lane) * V;
     const bool lane_ok = c0 < p.C_out;
     int w_out = 0, h_out = 0;
     long long img = pix;
     if (!p.is_fc) {
-        w_out = (int)(pix % p.W_out);
-        const long long r = pix / p.W_out;
-        h_out = (int)(r % p.H_out);
-        img = r / p.H_out;
+        const unsigned r = pix / (unsigned)p.W_out;
+        w_out = (int)(pix - r * (unsigned)p.W_out);
+        const unsigned q = r / (unsigned)p.H_out;
+        h_out = (int)(r - q * (unsigned)p.H_out);
+        img = q;
     }
     if (lane < ntaps) {
         long long col = -1;
@@ -329,7 +337,7 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
     if (p.fetched) {
         while (next_chunk < p.NC) account_one();
     }
-    if (lane_ok) stw<V>(p.out + pix * p.C_out + c0, nu.res);
+    if (lane_ok) stw<V>(p.out + (long long)pix * p.C_out + c0, nu.res);
     if (p.fetched) {
 #pragma unroll
         for (int dd = 16; dd > 0; dd >>= 1) fetched += __shfl_down_sync(FULL, fetched, dd);
@@ -344,7 +352,7 @@ int pick_v_dense(int C_out) {
 }
 
 template <int V, int R>
-cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t s, long long n_warps,
+cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t s, int n_warps,
                             int groups) {
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
     const size_t smem = (size_t)DW * dense_words(ntaps * p.C_in, p.T, ntaps) * sizeof(int) +
@@ -356,7 +364,7 @@ cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t 
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    kern<<<(unsigned)((n_warps + DW - 1) / DW), DW * 32, smem, s>>>(p, in, n_warps, groups);
+    kern<<<(n_warps + DW - 1) / DW, DW * 32, smem, s>>>(p, in, n_warps, groups);
     return cudaGetLastError();
 }
 
@@ -366,13 +374,14 @@ cudaError_t launch_dense_v(const IntegParams& p, const float* in, cudaStream_t s
     const long long pixels = p.is_fc ? (long long)p.B : (long long)p.B * p.H_out * p.W_out;
     const long long n_warps = pixels * groups;
     if (n_warps <= 0) return cudaSuccess;
+    if (n_warps >= (1ll << 31)) return cudaErrorInvalidValue;   // 32-bit work index
     const int fan = (p.is_fc ? 1 : p.K * p.K) * p.C_in;
     const int w = (fan + 31) / 32;                          // 32-input windows per pixel
-    if (w <= 1) return launch_dense_vr<V, 1>(p, in, s, n_warps, groups);
-    if (w <= 4) return launch_dense_vr<V, 4>(p, in, s, n_warps, groups);
-    if (w <= 9) return launch_dense_vr<V, 9>(p, in, s, n_warps, groups);
-    if (w <= 18) return launch_dense_vr<V, 18>(p, in, s, n_warps, groups);
-    return launch_dense_vr<V, DENSE_WIN>(p, in, s, n_warps, groups);
+    if (w <= 1) return launch_dense_vr<V, 1>(p, in, s, (int)n_warps, groups);
+    if (w <= 4) return launch_dense_vr<V, 4>(p, in, s, (int)n_warps, groups);
+    if (w <= 9) return launch_dense_vr<V, 9>(p, in, s, (int)n_warps, groups);
+    if (w <= 18) return launch_dense_vr<V, 18>(p, in, s, (int)n_warps, groups);
+    return launch_dense_vr<V, DENSE_WIN>(p, in, s, (int)n_warps, groups);
 }
 
 }  // namespace

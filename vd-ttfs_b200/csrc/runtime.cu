@@ -161,6 +161,7 @@ struct vdt_ctx {
     bool counting = false;
     bool profiling = false;
     int dense_max_fan = 1152;        // layers with K*K*C_in up to this use k_dense
+    std::vector<int> kernel_override;  // per layer: -1 automatic, else VDT_KERNEL_*
     std::map<GraphKey, cudaGraphExec_t> cache;
     // profiling: (layer, stage, start, stop) per timed launch, read back lazily
     struct Mark { int layer, stage; cudaEvent_t a, b; };
@@ -172,8 +173,10 @@ struct vdt_ctx {
 namespace {
 // which integrator runs a layer: k_dense (bucketing fused in) for small
 // per-pixel fan-in, else k_sorted, else the generic chunk integrator
-int layer_kernel(const vdt_ctx* c, const Layer& ly, const vdt_time_cfg& cfg) {
+int layer_kernel(const vdt_ctx* c, int li, const vdt_time_cfg& cfg) {
+    const Layer& ly = c->m->layers[li];
     if (ly.d.out == VDT_OUT_VMEM) return VDT_KERNEL_VMEM;
+    if (li < (int)c->kernel_override.size() && c->kernel_override[li] >= 0) return c->kernel_override[li];
     const int fc = ly.d.kind == VDT_FC;
     const int K = fc ? 1 : ly.d.k;
     const int fan = K * K * ly.C_in;
@@ -487,7 +490,7 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
             ip.lut_mode = cfg.lut_mode; ip.decay_len = cfg.decay_len;
             ip.tfs = cfg.fire_start; ip.inf_time = cfg.inf_time;
             ip.fetched = fe;
-            const int kern = layer_kernel(c, ly, cfg);
+            const int kern = layer_kernel(c, i, cfg);
             const bool dense = kern == VDT_KERNEL_DENSE;
             if (!dense || ev) {
                 // the dense path needs no buckets; they are still built when
@@ -630,7 +633,36 @@ extern "C" int vdt_ctx_layer_kernels(const vdt_ctx* c, int n_layers, int* kernel
     g_last_error.clear();
     if (!c || !kernels) return fail(VDT_ERR_INVALID, "ctx or kernels is NULL");
     if (n_layers != (int)c->m->layers.size()) return fail(VDT_ERR_INVALID, "n_layers mismatch");
-    for (int i = 0; i < n_layers; ++i) kernels[i] = layer_kernel(c, c->m->layers[i], c->m->cfg);
+    for (int i = 0; i < n_layers; ++i) kernels[i] = layer_kernel(c, i, c->m->cfg);
+    return VDT_OK;
+}
+
+extern "C" int vdt_ctx_set_layer_kernel(vdt_ctx* c, int layer, int kernel) {
+    g_last_error.clear();
+    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    if (layer < 0 || layer >= (int)c->m->layers.size()) return fail(VDT_ERR_INVALID, "layer=%d", layer);
+    const Layer& ly = c->m->layers[layer];
+    const vdt_time_cfg& cfg = c->m->cfg;
+    const int fc = ly.d.kind == VDT_FC;
+    const int K = fc ? 1 : ly.d.k;
+    bool ok = false;
+    switch (kernel) {
+        case -1: ok = true; break;
+        case VDT_KERNEL_CHUNK: ok = ly.d.out != VDT_OUT_VMEM && integrate_supported(K, fc, cfg.delta, ly.C_out, cfg.T, cfg.decay_len); break;
+        case VDT_KERNEL_SORTED: ok = ly.d.out != VDT_OUT_VMEM && sorted_supported(K, fc, cfg.delta, ly.C_in, cfg.T, cfg.decay_len); break;
+        case VDT_KERNEL_DENSE: ok = ly.d.out != VDT_OUT_VMEM && dense_supported(K, fc, ly.C_in, cfg.T, cfg.decay_len); break;
+        case VDT_KERNEL_VMEM: ok = ly.d.out == VDT_OUT_VMEM; break;
+        default: return fail(VDT_ERR_INVALID, "kernel=%d", kernel);
+    }
+    if (!ok) return fail(VDT_ERR_UNSUPPORTED, "kernel %d cannot run layer %d", kernel, layer);
+    if (c->kernel_override.size() != c->m->layers.size()) c->kernel_override.assign(c->m->layers.size(), -1);
+    if (c->kernel_override[layer] != kernel) {
+        DeviceGuard g(c->m->device);
+        VDT_CUDA(cudaStreamSynchronize(c->stream));
+        for (auto& kv : c->cache) cudaGraphExecDestroy(kv.second);   // captured with the old choice
+        c->cache.clear();
+        c->kernel_override[layer] = kernel;
+    }
     return VDT_OK;
 }
 

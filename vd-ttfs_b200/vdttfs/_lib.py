@@ -73,6 +73,7 @@ SIGNATURES = {
     "vdt_pool_min": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _vp]),
     "vdt_readout": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_float, _vp, _vp]),
     "vdt_ctx_layer_kernels": (C.c_int, [_vp, C.c_int, _vp]),
+    "vdt_ctx_set_layer_kernel": (C.c_int, [_vp, C.c_int, C.c_int]),
     "vdt_noalloc_scratch_bytes": (C.c_size_t, []),
     "vdt_conv_layer_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, C.c_int, C.c_int,
                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,

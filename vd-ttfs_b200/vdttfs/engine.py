@@ -28,7 +28,7 @@ import weakref
 import numpy as np
 
 from . import nets
-from ._lib import LayerDesc, NetDesc, TimeCfg, check, lib
+from ._lib import LayerDesc, NetDesc, TimeCfg, VdtError, check, lib
 from .blob import BlobLayer, write_blob
 
 LUT_DEVICE, LUT_HOST_LIBM = 0, 1
@@ -150,6 +150,10 @@ class Context:
         k = np.zeros(n, np.int32)
         check(lib().vdt_ctx_layer_kernels(self.h, n, k.ctypes.data), "vdt_ctx_layer_kernels")
         return [int(v) for v in k]
+
+    def set_layer_kernel(self, layer: int, kernel: int):
+        """Force one layer's integrator (KERNEL_*), or -1 for the automatic choice."""
+        check(lib().vdt_ctx_set_layer_kernel(self.h, layer, kernel), "vdt_ctx_set_layer_kernel")
 
     def infer(self, x, pixels: bool = False, out=None, pred=None):
         """x: CUDA tensor [B, H, W, C] (spike times, or pixels if `pixels`)."""
