@@ -10,119 +10,29 @@
 //   2. sort: a stable counting sort of the events by tb in shared memory
 //      (warp-aggregated histogram with __match_any_sync, exclusive scan over the
 //      T steps, ranked scatter).  The input order is (tap, channel), so inside
-//      each step the list keeps exactly the reference's FMA-chain order;
-//   3. stream: per event one broadcast LDS.64, one V-wide weight load, V FMAs
-//      into a single accumulator per neuron; when the step changes, the step is
-//      closed (carry += acc, threshold test) and steps without input are closed
-//      in O(1) per neuron (non-increasing threshold tables: a constant carry
-//      can fire in a run only if it reaches the run's last valid threshold).
+//      each step the list keeps exactly the reference's FMA-chain order; the
+//      non-empty steps become a run table;
+//   3. stream (stream_runs): per event one broadcast LDS.64, one V-wide weight
+//      load, V FMAs into a single accumulator per neuron; each run ends with
+//      the close of its step, steps without input are closed in O(log T).
 //      The warp stops once all its neurons fired.
 // The fetched-synapse counter keeps the reference's chunk accounting (events
 // of every chunk a neuron entered alive).
+#include "lanes.h"
 #include "vdt_internal.h"
 
 namespace vdt {
 namespace {
 
-constexpr unsigned FULL = 0xffffffffu;
-constexpr int DW = 4;        // warps per CTA
-constexpr int DSUB = 8;      // weight rows in flight per streamed batch
+constexpr int DW = 4;         // warps per CTA
 constexpr int DENSE_WIN = 36; // largest fan-in handled: 36 windows of 32 inputs
 
-template <int V>
-__device__ __forceinline__ void ldw(const float* p, float (&w)[V]) {
-    if constexpr (V == 1) {
-        w[0] = __ldg(p);
-    } else if constexpr (V == 2) {
-        const float2 v = __ldg(reinterpret_cast<const float2*>(p));
-        w[0] = v.x; w[1] = v.y;
-    } else {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(p));
-        w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-    }
-}
-
-template <int V>
-__device__ __forceinline__ void stw(float* p, const float (&r)[V]) {
-    if constexpr (V == 1) {
-        *p = r[0];
-    } else if constexpr (V == 2) {
-        *reinterpret_cast<float2*>(p) = make_float2(r[0], r[1]);
-    } else {
-        *reinterpret_cast<float4*>(p) = make_float4(r[0], r[1], r[2], r[3]);
-    }
-}
-
-// shared words per warp: list (int2 per input), step bins (T + 1, padded),
-// tap column bases (64-bit)
+// shared words per warp: event records (int2 per input), step bins (T + 1),
+// tap column bases (64-bit), runs (int2 per non-empty step)
 __host__ __device__ inline int dense_words(int fan_in, int T, int ntaps) {
-    return ((2 * fan_in + 3) & ~3) + ((T + 1 + 3) & ~3) + ((2 * ntaps + 3) & ~3);
+    const int runs = fan_in < T ? fan_in : T;
+    return ((2 * fan_in + 3) & ~3) + ((T + 1 + 3) & ~3) + ((2 * ntaps + 3) & ~3) + 2 * runs;
 }
-
-template <int V>
-struct DLane {
-    float carry[V], res[V], acc[V];
-    bool alive[V];
-    __device__ __forceinline__ bool any() const {
-        bool a = false;
-#pragma unroll
-        for (int v = 0; v < V; ++v) a |= alive[v];
-        return a;
-    }
-    __device__ __forceinline__ int live() const {
-        int n = 0;
-#pragma unroll
-        for (int v = 0; v < V; ++v) n += alive[v] ? 1 : 0;
-        return n;
-    }
-    __device__ __forceinline__ void close_step(int s, const float* s_th, int t_min) {
-        const float th = s_th[s];
-#pragma unroll
-        for (int v = 0; v < V; ++v) {
-            if (alive[v]) {
-                carry[v] += acc[v];
-                if (s >= t_min && carry[v] >= th && th >= 1e-5f) {
-                    res[v] = (float)s;
-                    alive[v] = false;
-                }
-            }
-            acc[v] = 0.0f;
-        }
-    }
-    __device__ __forceinline__ void close_empty(int a, int b, const float* s_th, int t_min, int t_floor,
-                                                bool monotone) {
-        if (a >= b) return;
-        if (monotone) {
-            const int lo = max(a, t_min), hi = min(b, t_floor);
-            if (lo >= hi) return;
-            const float mn = s_th[hi - 1];
-#pragma unroll
-            for (int v = 0; v < V; ++v) {
-                if (alive[v] && carry[v] >= mn) {
-                    // thresholds are non-increasing: the first step whose
-                    // threshold the constant carry reaches, by bisection
-                    int l = lo, h = hi - 1;
-                    while (l < h) {
-                        const int mid = (l + h) >> 1;
-                        if (carry[v] >= s_th[mid]) h = mid; else l = mid + 1;
-                    }
-                    res[v] = (float)l;
-                    alive[v] = false;
-                }
-            }
-        } else {
-            for (int t = a; t < b; ++t) {
-                const float th = s_th[t];
-#pragma unroll
-                for (int v = 0; v < V; ++v)
-                    if (alive[v] && t >= t_min && carry[v] >= th && th >= 1e-5f) {
-                        res[v] = (float)t;
-                        alive[v] = false;
-                    }
-            }
-        }
-    }
-};
 
 // flattened input index f = tap * C_in + c -> tap, via a float estimate and
 // one exact correction (f < 2^20, so the estimate is off by at most one)
@@ -133,10 +43,16 @@ __device__ __forceinline__ int tap_of(int f, int C_in, float inv) {
     return j;
 }
 
-template <int V, int R, int MINB>
+// weight rows in flight per streamed block: fewer for the widest fan-ins,
+// whose inputs take more registers during the sort
+template <int R>
+__host__ __device__ constexpr int dense_fs() { return R <= 18 ? 8 : 4; }
+
+template <int V, int R, int MINB, bool COUNT>
 __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const float* __restrict__ in,
                                                          int n_warps, int groups) {
     extern __shared__ __align__(16) int sm[];
+    __shared__ int s_floor, s_mono;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
     const int fan = ntaps * p.C_in;
@@ -145,20 +61,12 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
     int2* s_list = reinterpret_cast<int2*>(wb);
     int* s_bin = wb + ((2 * fan + 3) & ~3);                  // [T + 1]
     long long* s_col = reinterpret_cast<long long*>(s_bin + ((p.T + 1 + 3) & ~3));
+    int2* s_runs = reinterpret_cast<int2*>(reinterpret_cast<int*>(s_col) + ((2 * ntaps + 3) & ~3));
     float* s_decay = reinterpret_cast<float*>(sm + DW * words);
     float* s_th = s_decay + p.decay_len;
-    __shared__ int s_floor, s_mono;
+    float* s_thx = s_th + p.T;
     for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
-    for (int i = threadIdx.x; i < p.T; i += blockDim.x) s_th[i] = p.lut_th[i];
-    if (threadIdx.x == 0) { s_floor = p.T; s_mono = 1; }
-    __syncthreads();
-    for (int t = threadIdx.x; t < p.T; t += blockDim.x) {
-        if (!(s_th[t] >= 1e-5f)) atomicMin(&s_floor, t);
-        if (t + 1 < p.T && !(s_th[t + 1] <= s_th[t])) s_mono = 0;
-    }
-    __syncthreads();
-    const bool monotone = s_mono != 0;
-    const int t_floor = s_floor;
+    const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
 
     const int gw = blockIdx.x * DW + warp;
     if (gw >= n_warps) return;                               // warp-uniform
@@ -204,34 +112,37 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
             if (cb >= 0) tv[r] = __ldg(in + cb + (f - j * p.C_in));
         }
     }
-    // input value -> its step tb (or -1) and LUT value (bucketize rule)
-    auto decode = [&](float t, int& tb, float& lv) {
-        tb = -1;
-        if (!(t < p.inf_time)) return;
-        int b = (int)floorf(t - p.tfs);
-        if (b < 0) b = 0;
-        if (b >= p.T) return;
-        int ti;
-        if (p.lut_mode == VDT_LUT_BY_TB) {
-            ti = b;
-        } else {
-            ti = (int)t;
-            ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+    // input value -> key = tb | LUT index << 16 (bucketize rule), -1 if no event
+    int key[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const float t = tv[r];
+        key[r] = -1;
+        if (t < p.inf_time) {
+            int b = (int)floorf(t - p.tfs);
+            if (b < 0) b = 0;
+            if (b < p.T) {
+                int ti;
+                if (p.lut_mode == VDT_LUT_BY_TB) {
+                    ti = b;
+                } else {
+                    ti = (int)t;
+                    ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+                }
+                key[r] = b | (ti << 16);
+            }
         }
-        tb = b;
-        lv = s_decay[ti];
-    };
+    }
     // 1. histogram by step
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-        int tb;
-        float lv;
-        decode(tv[r], tb, lv);
-        const unsigned g = __match_any_sync(FULL, tb);
+        const int tb = key[r] < 0 ? -1 : (key[r] & 0xffff);
+        const unsigned g = __match_any_sync(FULL_MASK, tb);
         if (tb >= 0 && lane == __ffs(g) - 1) s_bin[tb] += __popc(g);
         __syncwarp();
     }
-    // 2. exclusive scan over steps, then the stable scatter
+    // 2. exclusive scan over steps, then the stable scatter of records
+    //    {element offset of the weight row, LUT value}
     int run = 0;
     for (int b0 = 0; b0 < p.T; b0 += 32) {
         const int b = b0 + lane;
@@ -239,110 +150,67 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
         int x = v;
 #pragma unroll
         for (int dd = 1; dd < 32; dd <<= 1) {
-            const int u = __shfl_up_sync(FULL, x, dd);
+            const int u = __shfl_up_sync(FULL_MASK, x, dd);
             if (lane >= dd) x += u;
         }
         if (b < p.T) s_bin[b] = run + x - v;
-        run += __shfl_sync(FULL, x, 31);
+        run += __shfl_sync(FULL_MASK, x, 31);
     }
-    const int n = run;
     __syncwarp();
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-        int tb;
-        float lv;
-        decode(tv[r], tb, lv);
-        const unsigned g = __match_any_sync(FULL, tb);
+        const int tb = key[r] < 0 ? -1 : (key[r] & 0xffff);
+        const unsigned g = __match_any_sync(FULL_MASK, tb);
         int pos = 0;
         if (tb >= 0) pos = s_bin[tb] + __popc(g & lt);
         __syncwarp();
         if (tb >= 0) {
-            s_list[pos] = make_int2((r * 32 + lane) | (tb << 20), __float_as_int(lv));
+            s_list[pos] = make_int2((r * 32 + lane) * p.C_out, __float_as_int(s_decay[key[r] >> 16]));
             if (lane == __ffs(g) - 1) s_bin[tb] += __popc(g);
         }
         __syncwarp();
     }
+    // s_bin[tb] is now the end of step tb's run
+    const int nruns = compact_runs(s_bin, p.T, 0, s_runs);
 
-    // 3. stream the step-ordered list
-    DLane<V> nu;
-#pragma unroll
-    for (int v = 0; v < V; ++v) {
-        nu.carry[v] = lane_ok ? __ldg(p.bias + c0 + v) : 0.0f;
-        nu.res[v] = p.inf_time;
-        nu.acc[v] = 0.0f;
-        nu.alive[v] = lane_ok;
-    }
+    // 3. stream the runs
+    Lanes<V> nu;
+    nu.init(p.bias, c0, lane_ok, p.inf_time);
     const float* Wl = p.W + (lane_ok ? c0 : 0);
-    const int C_out = p.C_out;
-    // fetched synapses, reference chunk accounting: the chunk sizes come from
-    // the scattered bins (s_bin[tb] now holds the end of step tb's run)
-    unsigned long long fetched = 0;
-    int next_chunk = 0;
-    auto step_end = [&](int t) { return t <= 0 ? 0 : s_bin[t - 1]; };   // events with tb < t
-    auto account_one = [&]() {
-        const int a = next_chunk * p.delta, b = min(p.T, a + p.delta);
-        fetched += (unsigned long long)(step_end(b) - step_end(a)) * nu.live();
-        ++next_chunk;
-    };
-    auto close_run = [&](int a, int b) {
-        if (p.fetched) {
-            while (next_chunk < p.NC && next_chunk * p.delta < b) {
-                const int cs = max(a, next_chunk * p.delta);
-                nu.close_empty(a, cs, s_th, p.t_min, t_floor, monotone);
-                a = cs;
-                account_one();
+    int next_t = 0;
+    if constexpr (!COUNT) {
+        if (stream_runs<V, dense_fs<R>()>(nu, s_list, 0, s_runs, nruns, Wl, next_t, tt))
+            nu.close_empty(next_t, p.T, tt);
+    } else {
+        // fetched synapses, reference chunk accounting: chunk c counts its
+        // events once per neuron still alive when the chunk starts
+        unsigned long long fetched = 0;
+        int next_chunk = 0;
+        auto step_end = [&](int t) { return t <= 0 ? 0 : s_bin[min(t, p.T) - 1]; };
+        auto account_to = [&](int t) {                       // every chunk starting at or before t
+            while (next_chunk < p.NC && next_chunk * p.delta <= t) {
+                const int cs = next_chunk * p.delta;
+                nu.close_empty(next_t, cs, tt);
+                next_t = max(next_t, cs);
+                fetched += (unsigned long long)(step_end(cs + p.delta) - step_end(cs)) * nu.live();
+                ++next_chunk;
             }
+        };
+        int k = 0;
+        for (int j = 0; j < nruns; ++j) {
+            const int2 rn = s_runs[j];
+            account_to(rn.y);
+            for (; k < rn.x; ++k) stream_block<V, 1>(nu, s_list + k, Wl);
+            nu.close_empty(next_t, rn.y, tt);
+            nu.close_step(rn.y, tt);
+            next_t = rn.y + 1;
         }
-        nu.close_empty(a, b, s_th, p.t_min, t_floor, monotone);
-    };
-
-    // runs of equal step: stream the run into acc, then close the step
-    int k = 0, next_t = 0;
-    while (k < n) {
-        const int tb = s_list[k].x >> 20;                     // warp-uniform
-        const int end = s_bin[tb];                            // end of tb's run
-        close_run(next_t, tb);
-        if (p.fetched) {
-            while (next_chunk < p.NC && next_chunk * p.delta <= tb) account_one();
-        }
-        if (!__any_sync(FULL, nu.any())) { next_t = p.T; break; }
-        const bool lane_live = nu.any();
-        float w[DSUB][V];
-        for (; k + DSUB <= end; k += DSUB) {
-            int2 e[DSUB];
+        nu.close_empty(next_t, p.T, tt);
 #pragma unroll
-            for (int u = 0; u < DSUB; ++u) e[u] = s_list[k + u];
-            if (lane_live) {
-#pragma unroll
-                for (int u = 0; u < DSUB; ++u) ldw<V>(Wl + (e[u].x & 0xfffff) * C_out, w[u]);
-            }
-#pragma unroll
-            for (int u = 0; u < DSUB; ++u) {
-                const float lq = __int_as_float(e[u].y);
-#pragma unroll
-                for (int v = 0; v < V; ++v) nu.acc[v] = fmaf(w[u][v], lq, nu.acc[v]);
-            }
-        }
-        for (; k < end; ++k) {
-            const int2 e = s_list[k];
-            if (lane_live) ldw<V>(Wl + (e.x & 0xfffff) * C_out, w[0]);
-            const float lq = __int_as_float(e.y);
-#pragma unroll
-            for (int v = 0; v < V; ++v) nu.acc[v] = fmaf(w[0][v], lq, nu.acc[v]);
-        }
-        nu.close_step(tb, s_th, p.t_min);
-        next_t = tb + 1;
-    }
-    close_run(next_t, p.T);
-    if (p.fetched) {
-        while (next_chunk < p.NC) account_one();
-    }
-    if (lane_ok) stw<V>(p.out + (long long)pix * p.C_out + c0, nu.res);
-    if (p.fetched) {
-#pragma unroll
-        for (int dd = 16; dd > 0; dd >>= 1) fetched += __shfl_down_sync(FULL, fetched, dd);
+        for (int dd = 16; dd > 0; dd >>= 1) fetched += __shfl_down_sync(FULL_MASK, fetched, dd);
         if (lane == 0 && fetched) atomicAdd(p.fetched, fetched);
     }
+    if (lane_ok) store_res<V>(p.out + (long long)pix * p.C_out + c0, nu.res);
 }
 
 int pick_v_dense(int C_out) {
@@ -356,10 +224,13 @@ cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t 
                             int groups) {
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
     const size_t smem = (size_t)DW * dense_words(ntaps * p.C_in, p.T, ntaps) * sizeof(int) +
-                        (size_t)(p.decay_len + p.T) * sizeof(float);
-    constexpr int REGS = DSUB * V + 4 * V + R + 56;
+                        (size_t)(p.decay_len + 2 * p.T) * sizeof(float);
+    // register budget tuned for occupancy (the kernel is latency-bound): the
+    // streamed block, lane state and the sort's input registers
+    constexpr int FS = dense_fs<R>();
+    constexpr int REGS = FS * V + 2 * FS + 4 * V + R;
     constexpr int MINB = (65536 / (DW * 32 * REGS)) > 8 ? 8 : (65536 / (DW * 32 * REGS));
-    auto kern = k_dense<V, R, MINB>;
+    auto kern = p.fetched ? k_dense<V, R, MINB, true> : k_dense<V, R, MINB, false>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
@@ -375,22 +246,25 @@ cudaError_t launch_dense_v(const IntegParams& p, const float* in, cudaStream_t s
     const long long n_warps = pixels * groups;
     if (n_warps <= 0) return cudaSuccess;
     if (n_warps >= (1ll << 31)) return cudaErrorInvalidValue;   // 32-bit work index
+    const int nw = (int)n_warps;
     const int fan = (p.is_fc ? 1 : p.K * p.K) * p.C_in;
     const int w = (fan + 31) / 32;                          // 32-input windows per pixel
-    if (w <= 1) return launch_dense_vr<V, 1>(p, in, s, (int)n_warps, groups);
-    if (w <= 4) return launch_dense_vr<V, 4>(p, in, s, (int)n_warps, groups);
-    if (w <= 9) return launch_dense_vr<V, 9>(p, in, s, (int)n_warps, groups);
-    if (w <= 18) return launch_dense_vr<V, 18>(p, in, s, (int)n_warps, groups);
-    return launch_dense_vr<V, DENSE_WIN>(p, in, s, (int)n_warps, groups);
+    if (w <= 1) return launch_dense_vr<V, 1>(p, in, s, nw, groups);
+    if (w <= 4) return launch_dense_vr<V, 4>(p, in, s, nw, groups);
+    if (w <= 9) return launch_dense_vr<V, 9>(p, in, s, nw, groups);
+    if (w <= 18) return launch_dense_vr<V, 18>(p, in, s, nw, groups);
+    return launch_dense_vr<V, DENSE_WIN>(p, in, s, nw, groups);
 }
 
 }  // namespace
 
-bool dense_supported(int K, int is_fc, int C_in, int T, int decay_len) {
+bool dense_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len) {
     const int ntaps = is_fc ? 1 : K * K;
     const int fan = ntaps * C_in;
-    if (ntaps > 32 || fan > DENSE_WIN * 32 || T >= 2048) return false;   // inputs held in registers
-    return (size_t)DW * dense_words(fan, T, ntaps) * sizeof(int) + (size_t)(decay_len + T) * sizeof(float) <=
+    if (ntaps > 32 || fan > DENSE_WIN * 32) return false;   // inputs held in registers
+    if ((long long)fan * C_out >= (1ll << 31)) return false; // 31-bit weight offsets
+    if (T > 0xffff) return false;                           // 16-bit step keys
+    return (size_t)DW * dense_words(fan, T, ntaps) * sizeof(int) + (size_t)(decay_len + 2 * T) * sizeof(float) <=
            160 * 1024;
 }
 

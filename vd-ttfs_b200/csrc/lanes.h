@@ -1,0 +1,215 @@
+// lanes.h -- per-lane neuron state shared by the integrators (k_dense,
+// k_sorted): V output channels per lane, the membrane carry, the open step's
+// accumulator and the first-spike result.
+//
+// Step semantics follow k_conv_bucketed (t1:150-157, t2:158-165): at the end
+// of step s the step's input (a per-step FMA chain, accumulated in `acc`) is
+// added to the carry with one separate add, and the neuron fires at s if
+// s >= t_min, LUT_th[s] >= 1e-5 and carry >= LUT_th[s].
+#pragma once
+
+#include "vdt_internal.h"
+
+namespace vdt {
+
+constexpr unsigned FULL_MASK = 0xffffffffu;
+
+// Staged threshold tables: s_th = LUT_th, s_thx = LUT_th where a spike may be
+// recorded (s >= t_min and LUT_th >= 1e-5), NaN elsewhere (every comparison
+// with NaN is false); t_floor = first step with LUT_th < 1e-5 (or T) and
+// monotone = thresholds non-increasing.  Built by the whole CTA.
+struct ThTables {
+    const float* th;
+    const float* thx;
+    int t_min, t_floor;
+    bool monotone;
+};
+
+__device__ __forceinline__ ThTables stage_thresholds(const IntegParams& p, float* s_th, float* s_thx,
+                                                     int* s_floor, int* s_mono) {
+    for (int i = threadIdx.x; i < p.T; i += blockDim.x) {
+        const float th = p.lut_th[i];
+        s_th[i] = th;
+        s_thx[i] = (i >= p.t_min && th >= 1e-5f) ? th : __int_as_float(0x7fffffff);
+    }
+    if (threadIdx.x == 0) { *s_floor = p.T; *s_mono = 1; }
+    __syncthreads();
+    for (int t = threadIdx.x; t < p.T; t += blockDim.x) {
+        if (!(s_th[t] >= 1e-5f)) atomicMin(s_floor, t);
+        if (t + 1 < p.T && !(s_th[t + 1] <= s_th[t])) *s_mono = 0;
+    }
+    __syncthreads();
+    return ThTables{s_th, s_thx, p.t_min, *s_floor, *s_mono != 0};
+}
+
+template <int V>
+struct Lanes {
+    float carry[V], res[V], acc[V];
+    bool alive[V];
+
+    __device__ __forceinline__ void init(const float* bias, int c0, bool lane_ok, float inf_time) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            carry[v] = lane_ok ? __ldg(bias + c0 + v) : 0.0f;
+            res[v] = inf_time;
+            acc[v] = 0.0f;
+            alive[v] = lane_ok;
+        }
+    }
+    __device__ __forceinline__ bool any() const {
+        bool a = false;
+#pragma unroll
+        for (int v = 0; v < V; ++v) a |= alive[v];
+        return a;
+    }
+    __device__ __forceinline__ int live() const {
+        int n = 0;
+#pragma unroll
+        for (int v = 0; v < V; ++v) n += alive[v] ? 1 : 0;
+        return n;
+    }
+    __device__ __forceinline__ void fma(const float (&w)[V], float lv) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) acc[v] = fmaf(w[v], lv, acc[v]);
+    }
+    // end of step s with input: carry += acc, threshold test, acc = 0
+    __device__ __forceinline__ void close_step(int s, const ThTables& tt) {
+        const float th = tt.thx[s];
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            if (alive[v]) {
+                carry[v] += acc[v];
+                if (carry[v] >= th) {
+                    res[v] = (float)s;
+                    alive[v] = false;
+                }
+            }
+            acc[v] = 0.0f;
+        }
+    }
+    // steps [a, b) without input: the carry is constant, so with
+    // non-increasing thresholds a neuron fires in the run iff it reaches the
+    // run's last valid threshold, at the first step found by bisection
+    __device__ __forceinline__ void close_empty(int a, int b, const ThTables& tt) {
+        if (a >= b) return;
+        if (tt.monotone) {
+            const int lo = max(a, tt.t_min), hi = min(b, tt.t_floor);
+            if (lo >= hi) return;
+            const float mn = tt.th[hi - 1];
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+                if (alive[v] && carry[v] >= mn) {
+                    int l = lo, h = hi - 1;
+                    while (l < h) {
+                        const int mid = (l + h) >> 1;
+                        if (carry[v] >= tt.th[mid]) h = mid; else l = mid + 1;
+                    }
+                    res[v] = (float)l;
+                    alive[v] = false;
+                }
+            }
+        } else {
+            for (int t = a; t < b; ++t) {
+                const float th = tt.thx[t];
+#pragma unroll
+                for (int v = 0; v < V; ++v)
+                    if (alive[v] && carry[v] >= th) {
+                        res[v] = (float)t;
+                        alive[v] = false;
+                    }
+            }
+        }
+    }
+};
+
+template <int V>
+__device__ __forceinline__ void load_row(const float* p, float (&w)[V]);
+
+// U records {element offset of the event's weight row, LUT value bits}:
+// U weight loads in flight, then the U FMAs of each neuron's chain in order
+template <int V, int U>
+__device__ __forceinline__ void stream_block(Lanes<V>& nu, const int2* rec, const float* Wl) {
+    int2 e[U];
+    float w[U][V];
+#pragma unroll
+    for (int u = 0; u < U; ++u) e[u] = rec[u];
+#pragma unroll
+    for (int u = 0; u < U; ++u) load_row<V>(Wl + (unsigned)e[u].x, w[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) nu.fma(w[u], __int_as_float(e[u].y));
+}
+
+// Stream step-sorted records through their runs: runs[j] = {end index of
+// run j in rec, its step}, runs in increasing step order, the records of one
+// run in FMA-chain order.  Full blocks of FS records run without any test;
+// a run's tail is split into blocks of 4, 2 and 1.  Each run ends with the
+// close of its step (input-free steps before it are closed first).  Returns
+// false once every neuron of the warp has fired (the caller may stop).
+template <int V, int FS>
+__device__ __forceinline__ bool stream_runs(Lanes<V>& nu, const int2* rec, int k, const int2* runs,
+                                            int nruns, const float* Wl, int& next_t,
+                                            const ThTables& tt) {
+    for (int j = 0; j < nruns; ++j) {
+        const int2 rn = runs[j];
+        const int end = rn.x;
+        for (; k + FS <= end; k += FS) stream_block<V, FS>(nu, rec + k, Wl);
+        if (end - k >= 4) { stream_block<V, 4>(nu, rec + k, Wl); k += 4; }
+        if (end - k >= 2) { stream_block<V, 2>(nu, rec + k, Wl); k += 2; }
+        if (end - k >= 1) { stream_block<V, 1>(nu, rec + k, Wl); k += 1; }
+        nu.close_empty(next_t, rn.y, tt);
+        nu.close_step(rn.y, tt);
+        next_t = rn.y + 1;
+        if (!__any_sync(FULL_MASK, nu.any())) return false;
+    }
+    return true;
+}
+
+// Compact the non-empty bins into runs: bins [0, nb) with exclusive ends
+// end[b] (start of bin b = end[b - 1], 0 for b = 0); runs[j] = {end, base + b}.
+// Returns the number of runs.  Whole warp.
+__device__ __forceinline__ int compact_runs(const int* end, int nb, int base, int2* runs) {
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = (1u << lane) - 1u;
+    int n = 0;
+    for (int b0 = 0; b0 < nb; b0 += 32) {
+        const int b = b0 + lane;
+        bool ne = false;
+        int e = 0;
+        if (b < nb) {
+            e = end[b];
+            ne = e > (b == 0 ? 0 : end[b - 1]);
+        }
+        const unsigned m = __ballot_sync(FULL_MASK, ne);
+        if (ne) runs[n + __popc(m & lt)] = make_int2(e, base + b);
+        n += __popc(m);
+    }
+    __syncwarp();
+    return n;
+}
+
+template <int V>
+__device__ __forceinline__ void load_row(const float* p, float (&w)[V]) {
+    if constexpr (V == 1) {
+        w[0] = __ldg(p);
+    } else if constexpr (V == 2) {
+        const float2 v = __ldg(reinterpret_cast<const float2*>(p));
+        w[0] = v.x; w[1] = v.y;
+    } else {
+        static_assert(V == 4, "V is 1, 2 or 4");
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+        w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    }
+}
+
+template <int V>
+__device__ __forceinline__ void store_res(float* p, const float (&r)[V]) {
+    if constexpr (V == 1) {
+        *p = r[0];
+    } else if constexpr (V == 2) {
+        *reinterpret_cast<float2*>(p) = make_float2(r[0], r[1]);
+    } else {
+        *reinterpret_cast<float4*>(p) = make_float4(r[0], r[1], r[2], r[3]);
+    }
+}
+
+}  // namespace vdt

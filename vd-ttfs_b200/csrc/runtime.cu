@@ -180,9 +180,9 @@ int layer_kernel(const vdt_ctx* c, int li, const vdt_time_cfg& cfg) {
     const int fc = ly.d.kind == VDT_FC;
     const int K = fc ? 1 : ly.d.k;
     const int fan = K * K * ly.C_in;
-    if (fan <= c->dense_max_fan && dense_supported(ly.d.k, fc, ly.C_in, cfg.T, cfg.decay_len))
+    if (fan <= c->dense_max_fan && dense_supported(ly.d.k, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len))
         return VDT_KERNEL_DENSE;
-    if (sorted_supported(K, fc, cfg.delta, ly.C_in, cfg.T, cfg.decay_len)) return VDT_KERNEL_SORTED;
+    if (sorted_supported(K, fc, kSortedDelta, ly.C_in, ly.C_out, cfg.T, cfg.decay_len)) return VDT_KERNEL_SORTED;
     return VDT_KERNEL_CHUNK;
 }
 
@@ -417,7 +417,8 @@ struct Sizes {
 
 Sizes ctx_sizes(const vdt_model* m, long long B) {
     Sizes s;
-    const int OS = (m->cfg.T + m->cfg.delta - 1) / m->cfg.delta + 1;
+    const int dmin = std::min(m->cfg.delta, kSortedDelta);
+    const int OS = (m->cfg.T + dmin - 1) / dmin + 1;
     s.act = (size_t)B * m->net.in_h * m->net.in_w * m->net.in_c;
     for (auto& ly : m->layers) {
         const size_t in = (size_t)B * ly.H_in * ly.W_in * ly.C_in;
@@ -449,7 +450,6 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
             float* const* trace) {
     const vdt_model* m = c->m;
     const vdt_time_cfg& cfg = m->cfg;
-    const int NC = (cfg.T + cfg.delta - 1) / cfg.delta;
     cudaStream_t s = c->stream;
     const float* x = d_input;
     int ai = 0;
@@ -486,11 +486,16 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
             ip.K = ly.d.k;
             ip.pad = (!fc && ly.d.pad == VDT_PAD_SAME) ? ly.d.k / 2 : 0;
             ip.is_fc = fc;
-            ip.T = cfg.T; ip.delta = cfg.delta; ip.NC = NC; ip.t_min = ly.t_min;
+            const int kern = layer_kernel(c, i, cfg);
+            // k_sorted buckets at its own chunk width (results do not depend
+            // on it); the counting pass keeps the configured width, which
+            // defines the reference's fetched-synapse accounting
+            const int kd = (kern == VDT_KERNEL_SORTED && !ev) ? kSortedDelta : cfg.delta;
+            const int knc = (cfg.T + kd - 1) / kd;
+            ip.T = cfg.T; ip.delta = kd; ip.NC = knc; ip.t_min = ly.t_min;
             ip.lut_mode = cfg.lut_mode; ip.decay_len = cfg.decay_len;
             ip.tfs = cfg.fire_start; ip.inf_time = cfg.inf_time;
             ip.fetched = fe;
-            const int kern = layer_kernel(c, i, cfg);
             const bool dense = kern == VDT_KERNEL_DENSE;
             if (!dense || ev) {
                 // the dense path needs no buckets; they are still built when
@@ -502,8 +507,8 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
                 bp.layout = VDT_LAYOUT_NHWC;
                 bp.hw = 1;
                 bp.T = cfg.T;
-                bp.delta = cfg.delta;
-                bp.NC = NC;
+                bp.delta = kd;
+                bp.NC = knc;
                 bp.tfs = cfg.fire_start;
                 bp.tb_mode = VDT_TB_FLOOR_STAGGER;
                 bp.inf_time = cfg.inf_time;
@@ -649,8 +654,8 @@ extern "C" int vdt_ctx_set_layer_kernel(vdt_ctx* c, int layer, int kernel) {
     switch (kernel) {
         case -1: ok = true; break;
         case VDT_KERNEL_CHUNK: ok = ly.d.out != VDT_OUT_VMEM && integrate_supported(K, fc, cfg.delta, ly.C_out, cfg.T, cfg.decay_len); break;
-        case VDT_KERNEL_SORTED: ok = ly.d.out != VDT_OUT_VMEM && sorted_supported(K, fc, cfg.delta, ly.C_in, cfg.T, cfg.decay_len); break;
-        case VDT_KERNEL_DENSE: ok = ly.d.out != VDT_OUT_VMEM && dense_supported(K, fc, ly.C_in, cfg.T, cfg.decay_len); break;
+        case VDT_KERNEL_SORTED: ok = ly.d.out != VDT_OUT_VMEM && sorted_supported(K, fc, kSortedDelta, ly.C_in, ly.C_out, cfg.T, cfg.decay_len); break;
+        case VDT_KERNEL_DENSE: ok = ly.d.out != VDT_OUT_VMEM && dense_supported(K, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len); break;
         case VDT_KERNEL_VMEM: ok = ly.d.out == VDT_OUT_VMEM; break;
         default: return fail(VDT_ERR_INVALID, "kernel=%d", kernel);
     }

@@ -55,12 +55,14 @@ bool integrate_supported(int K, int is_fc, int delta, int C_out, int T, int deca
 // Integrator fused with the bucketing for small per-pixel fan-in: reads the
 // NHWC spike map `in` directly (same results as bucketize + integrate).
 cudaError_t launch_dense(const IntegParams& p, const float* in, cudaStream_t s);
-bool dense_supported(int K, int is_fc, int C_in, int T, int decay_len);
+bool dense_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len);
 
 // Chunk integrator with per-chunk slot sorting (reference bucket layout,
 // same results as launch_integrate, fewer instructions per event).
 cudaError_t launch_sorted(const IntegParams& p, cudaStream_t s);
-bool sorted_supported(int K, int is_fc, int delta, int C_in, int T, int decay_len);
+// chunk width the runtime buckets k_sorted layers at (outside counting passes)
+constexpr int kSortedDelta = 8;
+bool sorted_supported(int K, int is_fc, int delta, int C_in, int C_out, int T, int decay_len);
 
 // -------------------------------------------------------------- edges / LUT
 struct LutJob {            // one layer's table pair
