@@ -87,6 +87,43 @@ struct Lanes {
             acc[v] = 0.0f;
         }
     }
+    // branch-free forms of the two closes (no per-lane divergence): a dead
+    // neuron's carry is never read again, so it is updated unconditionally
+    __device__ __forceinline__ void close_step_bf(int s, const ThTables& tt) {
+        const float th = tt.thx[s];
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            carry[v] += acc[v];
+            const bool fire = alive[v] && carry[v] >= th;
+            res[v] = fire ? (float)s : res[v];
+            alive[v] = alive[v] && !fire;
+            acc[v] = 0.0f;
+        }
+    }
+    // steps [a, b) without input, non-increasing thresholds: the first step
+    // t in [lo, hi) with carry >= LUT_th[t] by a bisection whose trip count
+    // depends only on the (warp-uniform) run length
+    __device__ __forceinline__ void close_empty_bf(int a, int b, const ThTables& tt) {
+        if (a >= b) return;
+        if (!tt.monotone) { close_empty(a, b, tt); return; }
+        const int lo = max(a, tt.t_min), hi = min(b, tt.t_floor);
+        if (lo >= hi) return;
+        const float mn = tt.th[hi - 1];
+        int top = 1;
+        while (top * 2 <= hi - lo) top *= 2;
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            // pos = last step in [lo - 1, hi - 1) whose threshold is above the carry
+            int pos = lo - 1;
+            for (int step = top; step > 0; step >>= 1) {
+                const int q = pos + step;
+                pos = (q < hi && tt.th[q] > carry[v]) ? q : pos;
+            }
+            const bool fire = alive[v] && carry[v] >= mn;
+            res[v] = fire ? (float)(pos + 1) : res[v];
+            alive[v] = alive[v] && !fire;
+        }
+    }
     // steps [a, b) without input: the carry is constant, so with
     // non-increasing thresholds a neuron fires in the run iff it reaches the
     // run's last valid threshold, at the first step found by bisection
@@ -125,6 +162,37 @@ struct Lanes {
 template <int V>
 __device__ __forceinline__ void load_row(const float* p, float (&w)[V]);
 
+// one record {weight offset, LUT value} from a 32-bit shared-memory address
+__device__ __forceinline__ int2 lds_rec(unsigned sa) {
+    int2 e;
+    asm volatile("ld.shared.v2.s32 {%0, %1}, [%2];" : "=r"(e.x), "=r"(e.y) : "r"(sa));
+    return e;
+}
+
+// acc[v] = fma(w[v], lv, acc[v]) for every v; pairs use the packed
+// fma.rn.f32x2 (two independent round-to-nearest fp32 FMAs, the same
+// results as two fmaf calls)
+template <int V>
+__device__ __forceinline__ void fma_lanes(float (&acc)[V], const float (&w)[V], float lv) {
+    if constexpr (V == 1) {
+        acc[0] = fmaf(w[0], lv, acc[0]);
+    } else {
+#pragma unroll
+        for (int v = 0; v < V; v += 2) {
+            asm("{\n\t"
+                ".reg .b64 a, b, c;\n\t"
+                "mov.b64 a, {%0, %1};\n\t"
+                "mov.b64 b, {%2, %3};\n\t"
+                "mov.b64 c, {%4, %4};\n\t"
+                "fma.rn.f32x2 a, b, c, a;\n\t"
+                "mov.b64 {%0, %1}, a;\n\t"
+                "}"
+                : "+f"(acc[v]), "+f"(acc[v + 1])
+                : "f"(w[v]), "f"(w[v + 1]), "f"(lv));
+        }
+    }
+}
+
 // U records {element offset of the event's weight row, LUT value bits}:
 // U weight loads in flight, then the U FMAs of each neuron's chain in order
 template <int V, int U>
@@ -136,7 +204,20 @@ __device__ __forceinline__ void stream_block(Lanes<V>& nu, const int2* rec, cons
 #pragma unroll
     for (int u = 0; u < U; ++u) load_row<V>(Wl + (unsigned)e[u].x, w[u]);
 #pragma unroll
-    for (int u = 0; u < U; ++u) nu.fma(w[u], __int_as_float(e[u].y));
+    for (int u = 0; u < U; ++u) fma_lanes<V>(nu.acc, w[u], __int_as_float(e[u].y));
+}
+
+// the same from a 32-bit shared address (no generic-pointer arithmetic)
+template <int V, int U>
+__device__ __forceinline__ void stream_block_sa(Lanes<V>& nu, unsigned sa, const float* Wl) {
+    int2 e[U];
+    float w[U][V];
+#pragma unroll
+    for (int u = 0; u < U; ++u) e[u] = lds_rec(sa + 8u * u);
+#pragma unroll
+    for (int u = 0; u < U; ++u) load_row<V>(Wl + (unsigned)e[u].x, w[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) fma_lanes<V>(nu.acc, w[u], __int_as_float(e[u].y));
 }
 
 // Stream step-sorted records through their runs: runs[j] = {end index of
@@ -149,15 +230,16 @@ template <int V, int FS>
 __device__ __forceinline__ bool stream_runs(Lanes<V>& nu, const int2* rec, int k, const int2* runs,
                                             int nruns, const float* Wl, int& next_t,
                                             const ThTables& tt) {
+    const unsigned sa0 = (unsigned)__cvta_generic_to_shared(rec);
     for (int j = 0; j < nruns; ++j) {
         const int2 rn = runs[j];
         const int end = rn.x;
-        for (; k + FS <= end; k += FS) stream_block<V, FS>(nu, rec + k, Wl);
-        if (end - k >= 4) { stream_block<V, 4>(nu, rec + k, Wl); k += 4; }
-        if (end - k >= 2) { stream_block<V, 2>(nu, rec + k, Wl); k += 2; }
-        if (end - k >= 1) { stream_block<V, 1>(nu, rec + k, Wl); k += 1; }
+        for (; k + FS <= end; k += FS) stream_block_sa<V, FS>(nu, sa0 + 8u * k, Wl);
+        if (end - k >= 4) { stream_block_sa<V, 4>(nu, sa0 + 8u * k, Wl); k += 4; }
+        if (end - k >= 2) { stream_block_sa<V, 2>(nu, sa0 + 8u * k, Wl); k += 2; }
+        if (end - k >= 1) { stream_block_sa<V, 1>(nu, sa0 + 8u * k, Wl); k += 1; }
         nu.close_empty(next_t, rn.y, tt);
-        nu.close_step(rn.y, tt);
+        nu.close_step_bf(rn.y, tt);
         next_t = rn.y + 1;
         if (!__any_sync(FULL_MASK, nu.any())) return false;
     }
