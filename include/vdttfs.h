@@ -218,6 +218,55 @@ int vdt_readout(const float* d_out, int B, int K, int mode, float inf_time,
                 int32_t* d_pred, vdt_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Task 3 (DVS gesture) CuLIF stages.  Every neuron steps
+ * I = fma(I, decay, in[t]); V += I and fires at the first t with V >= th;
+ * the scan covers whole chunks (t < ceil(T/delta)*delta, as the reference).
+ * Spike maps are fp32 spike times (9999 = none).  Buckets come from
+ * vdt_bucketize with VDT_TB_TRUNC (NCHW sites for convs, per-sample rows for
+ * FC layers).
+ * ---------------------------------------------------------------------- */
+
+/* conv1_raw_early (t3:30-65): dense frames [N, C_in, H, W, T] (time
+   innermost), weights OIHW [C_out, C_in, K, K], same-pad conv; output NCHW.
+   in[t] sums w * frame in (c_in, ky, kx) order with FMAs; frames past T
+   read as 0.  delta in {8, 16, 32}, C_out <= 128. */
+int vdt_dvs_conv1_raw(const float* d_frames, const float* d_w_oihw, int N, int C_in, int C_out,
+                      int H, int W, int K, int T, int delta, float decay, float th, float* d_out,
+                      vdt_stream stream);
+
+/* conv_bucketed_early (t3:109-143): in[tt - base] += w over the chunk's
+   events in (ky, kx, bucket) order.  Weights HWIO [K, K, C_in, C_out]
+   (vdt_oihw_to_hwio converts the reference's OIHW); output NCHW or NHWC. */
+int vdt_dvs_conv_bucketed(const int* d_off, const int* d_cin, const float* d_tin,
+                          const float* d_w_hwio, int N, int C_in, int C_out, int H, int W, int K,
+                          int T, int delta, float decay, float th, int out_layout, float* d_out,
+                          vdt_stream stream);
+
+/* pool_chunk_early (t3:146-168): spiking 2x2 pool, in[t] = 1 at each input
+   spike's bin; layout VDT_LAYOUT_NCHW or VDT_LAYOUT_NHWC (in and out). */
+int vdt_dvs_pool(const float* d_in, float* d_out, int N, int C, int H_in, int W_in, int layout,
+                 int T, int delta, float decay, float th, vdt_stream stream);
+
+/* fc1_bucketed_recurrent (t3:171-200): feed-forward in_ff from the sample's
+   buckets plus, every step, the recurrent input of the neurons that fired
+   on the previous step (ascending j); I = fma(I, decay, in_ff) + in_rec; a
+   neuron fires once (V reset to -10000); no early exit.  Transposed weights:
+   d_w_t[j][i] = W_fc1[i][j] ([F_in, F_out]), d_wrec_t[j][i] = W_rec[i][j].
+   F_out a multiple of 32, at most 1024. */
+int vdt_dvs_fc1_recurrent(const int* d_off, const int* d_cin, const float* d_tin,
+                          const float* d_w_t, const float* d_wrec_t, int N, int F_in, int F_out,
+                          int T, int delta, float decay, float th, float* d_out, vdt_stream stream);
+
+/* fc2_bucketed_early (t3:203-225): bucketed FC, transposed weights
+   d_w_t[j][i] = W_fc2[i][j] ([F_in, F_out]); output [N, F_out]. */
+int vdt_dvs_fc2(const int* d_off, const int* d_cin, const float* d_tin, const float* d_w_t, int N,
+                int F_in, int F_out, int T, int delta, float decay, float th, float* d_out,
+                vdt_stream stream);
+
+/* OIHW [O, I, K, K] -> HWIO [K, K, I, O] weight permutation (device). */
+int vdt_oihw_to_hwio(const float* d_src, float* d_dst, int O, int I, int K, vdt_stream stream);
+
+/* ------------------------------------------------------------------------
  * Allocation-free layer step (no counterpart in the reference)
  * ---------------------------------------------------------------------- */
 

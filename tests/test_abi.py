@@ -32,6 +32,17 @@ def test_library_exports_every_declared_symbol():
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
 
 
+def test_ctypes_signatures_match_the_header():
+    """Every ctypes signature has as many arguments as the header declares."""
+    from vdttfs import _lib
+    src = open(os.path.join(ROOT, "include", "vdttfs.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    for m in re.finditer(r"\b(vdt_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", src, flags=re.S):
+        name, params = m.group(1), " ".join(m.group(2).split())
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert len(_lib.SIGNATURES[name][1]) == n, f"{name}: header has {n} parameters"
+
+
 def test_status_strings_and_version():
     from vdttfs import _lib
     L = _lib.lib()

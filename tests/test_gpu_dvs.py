@@ -1,0 +1,132 @@
+"""Task 3 (DVS gesture, CuLIF) on the GPU: every stage through the C ABI,
+bit-exact against the golden maps of the reference's own kernels and against
+the CPU oracle (oracle/vdt_oracle.c, orc_dvs_*) on seeded inputs.  Spike times
+are integers and the CuLIF arithmetic is a fixed FMA/add sequence, so the
+tolerance is zero."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from helpers import INF, bits_equal, spike_map
+
+sys.path.insert(0, os.path.join(GOLDEN))
+from make_golden import DVS_GAINS  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _np(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.detach().cpu().numpy()
+
+
+def test_dvs_ref_network_matches_the_reference_kernels(dev):
+    """The reference's own 2x32x32 DVS network: all seven stage maps equal the
+    golden maps produced by the reference's kernels, bit for bit."""
+    from vdttfs import dvs, nets, synth
+    g = np.load(os.path.join(GOLDEN, "net_dvs_ref.npz"))
+    spec = nets.dvs_ref()
+    wts = synth.dvs_weights(spec, 4, gains=DVS_GAINS)
+    w = dvs.DvsWeights(spec, wts, dev)
+    r = dvs.run(spec, w, _t(g["frames"].astype(np.float32), dev), keep=True)
+    for i, m in enumerate(r["maps"]):
+        assert bits_equal(_np(m).reshape(-1), g[f"map{i}"].astype(np.float32)), f"stage {i} differs"
+    ref_out = g["map6"].astype(np.float32).reshape(2, spec.classes)
+    want = np.array([np.argmin(o) for o in ref_out])           # lowest index among the minima
+    assert np.array_equal(_np(r["pred"]), want)
+
+
+@pytest.mark.parametrize("delta", [8, 16, 32, 64])
+def test_conv_bucketed_early_every_delta(O, dev, delta):
+    from vdttfs import dvs, nets
+    spec = nets.dvs_ref(delta=delta)
+    rng = np.random.default_rng(delta)
+    N, C_in, C_out, H, W = 2, 48, 96, 9, 7
+    x = spike_map(rng, (N, C_in, H, W), fire=0.35, T=spec.T, edges=True)
+    w = (rng.standard_normal((C_out, C_in, 3, 3)) * 0.35).astype(np.float32)
+    off, cin, tin, _ = O.bucketize(x, N * H * W, C_in, spec.T, delta, 0.0, 1, 1, H * W)
+    ref = np.empty(N * C_out * H * W, np.float32)
+    fe = O.lib().orc_dvs_conv(O._i(off), O._i(cin), O._f(tin), O._f(w), N, C_in, C_out, H, W, 3, spec.T, delta,
+                              spec.decay_conv, spec.th_conv, O._f(ref))
+    assert fe > 0
+    b = dvs.bucketize_sites(_t(x, dev), N, C_in, H, W, spec)
+    wd = dvs.oihw_to_hwio(_t(w, dev))
+    out = dvs.conv_bucketed(b, wd, N, C_in, C_out, H, W, spec)
+    got = _np(out)
+    assert bits_equal(got, ref), f"{np.sum(got != ref)} of {ref.size} differ"
+    assert 0.0 < np.mean(ref < INF) < 1.0
+    # NHWC output holds the same values
+    out2 = dvs.conv_bucketed(b, wd, N, C_in, C_out, H, W, spec, out_layout=0)
+    nhwc = _np(out2).reshape(N, H, W, C_out).transpose(0, 3, 1, 2).reshape(-1)
+    assert bits_equal(nhwc, ref)
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_pool_chunk_early(O, dev, layout):
+    from vdttfs import dvs, nets
+    spec = nets.dvs_ref()
+    rng = np.random.default_rng(3 + layout)
+    N, Cc, H, W = 3, 40, 10, 6
+    x = spike_map(rng, (N, Cc, H, W), fire=0.5, T=spec.T, edges=True)
+    ref = O.dvs_pool(x, N, Cc, H, W, spec)
+    xin = x if layout == 1 else x.transpose(0, 2, 3, 1)
+    got = _np(dvs.pool(_t(xin, dev), N, Cc, H, W, spec, layout=layout))
+    if layout == 0:
+        got = got.reshape(N, H // 2, W // 2, Cc).transpose(0, 3, 1, 2).reshape(-1)
+    assert bits_equal(got, ref)
+    assert np.mean(ref < INF) > 0.05
+
+
+def test_fc1_recurrent_and_fc2(O, dev):
+    from vdttfs import dvs, nets, synth
+    spec = nets.dvs_ref()
+    rng = np.random.default_rng(11)
+    N, F_in, F_out, K = 5, 700, 128, 11
+    x = spike_map(rng, (N, F_in), fire=0.3, T=spec.T, edges=True)
+    w = (rng.standard_normal((F_out, F_in)) * 0.25).astype(np.float32)
+    wr = (rng.standard_normal((F_out, F_out)) * 0.5).astype(np.float32)
+    ref1, _ = O.dvs_fc1(x, w, wr, N, F_in, F_out, spec)
+    b = dvs.bucketize_rows(_t(x, dev), N, F_in, spec)
+    got1 = _np(dvs.fc1_recurrent(b, _t(w.T, dev), _t(wr.T, dev), N, F_in, F_out, spec))
+    assert bits_equal(got1, ref1)
+    assert 0.0 < np.mean(ref1 < INF) < 1.0
+    w2 = (rng.standard_normal((K, F_out)) * 0.8).astype(np.float32)
+    ref2, fe, _ = O.dvs_fc2(ref1, w2, N, F_out, K, spec)
+    b2 = dvs.bucketize_rows(_t(ref1, dev), N, F_out, spec)
+    got2 = _np(dvs.fc2(b2, _t(w2.T, dev), N, F_out, K, spec))
+    assert bits_equal(got2, ref2)
+
+
+@pytest.mark.parametrize("delta", [8, 16, 32])
+def test_conv1_raw_early(O, dev, delta):
+    from vdttfs import dvs, nets, synth
+    spec = nets.dvs_ref(delta=delta)
+    spec = nets.DvsSpec(name="t", H=12, W=9, T=spec.T, delta=delta)
+    frames = synth.dvs_frames(4, 2, spec, stream=delta)
+    w = (np.random.default_rng(delta).standard_normal((spec.convs[0], 2, 3, 3)) * 2.0).astype(np.float32)
+    ref = O.dvs_conv1(frames, w, spec, 2)
+    got = _np(dvs.conv1_raw(_t(frames, dev), _t(w, dev), spec))
+    assert bits_equal(got.reshape(-1), ref)
+    assert 0.0 < np.mean(ref < INF) < 1.0
+
+
+def test_dvs_full_size_network_equals_oracle(O, dev):
+    """The 2x128x128 / 11-class configuration of the benchmark, one sample."""
+    from vdttfs import dvs, nets, synth
+    spec = nets.dvs()
+    wts = synth.dvs_weights(spec, 4)
+    frames = synth.dvs_frames(4, 1, spec, stream=1)
+    ref = O.run_dvs(spec, wts, frames, keep=True)
+    r = dvs.run(spec, dvs.DvsWeights(spec, wts, dev), _t(frames, dev), keep=True)
+    for i, (a, b) in enumerate(zip(r["maps"], ref["maps"])):
+        assert bits_equal(_np(a).reshape(-1), b), f"stage {i} differs"
+    assert np.array_equal(_np(r["pred"]), ref["pred"])

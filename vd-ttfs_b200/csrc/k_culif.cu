@@ -1,0 +1,300 @@
+// k_culif.cu -- task-3 (DVS gesture) CuLIF layers that are not bucketed
+// integrators: the raw-frame first convolution, the spiking 2x2 pool and the
+// recurrent FC1.  Same results as the reference kernels, bit for bit:
+//   conv1_raw_early        t3:30-65
+//   pool_chunk_early       t3:146-168
+//   fc1_bucketed_recurrent t3:171-200
+// (the bucketed conv / fc2 layers run on k_sorted, launch_culif).
+//
+// CuLIF step (every kernel): I = fma(I, decay, in[t]); V += I; fire at the
+// first t with V >= th.  The scan covers whole chunks (t < NC*delta, no t < T
+// guard, as in the reference).
+#include "lanes.h"
+#include "vdt_internal.h"
+
+namespace vdt {
+namespace {
+
+// ------------------------------------------------------------ conv1 (raw) --
+// One warp per output pixel (n, y, x), lane l owns output channels
+// l*V .. l*V+V-1.  Per chunk the pixel's K*K*C_in input frame windows (delta
+// time bins each, contiguous in memory: frames are [N, C_in, H, W, T]) are
+// staged in shared memory; every lane then forms in[t] for its channels with
+// the reference's FMA order (c_in, ky, kx; out-of-range taps skipped) and
+// scans the chunk.  Frames past T read as 0.
+constexpr int C1_WARPS = 4;
+
+template <int V, int DELTA>
+__global__ void __launch_bounds__(C1_WARPS * 32) k_culif_conv1(const float* __restrict__ frames,
+                                                               const float* __restrict__ w_oihw,
+                                                               float* __restrict__ out, int N, int C_in,
+                                                               int C_out, int H, int W, int K, int T,
+                                                               int NC, float decay, float th) {
+    extern __shared__ float c1_sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int taps = C_in * K * K;
+    float* s_f = c1_sm + warp * taps * DELTA;                 // [taps][DELTA]
+    const long long gw = (long long)blockIdx.x * C1_WARPS + warp;
+    if (gw >= (long long)N * H * W) return;
+    const int x = (int)(gw % W);
+    const int y = (int)((gw / W) % H);
+    const long long n = gw / ((long long)W * H);
+    const int pad = K / 2;
+    const int c0 = lane * V;
+    const bool lane_ok = c0 < C_out;
+
+    CulifLanes<V> nu;
+    nu.init(lane_ok, 9999.0f);
+    const CulifCfg cc{decay, th};
+    for (int tau = 0; tau < NC; ++tau) {
+        const int base = tau * DELTA;
+        // stage: tap q = (ci*K + ky)*K + kx, bin t -> frame value (0 when the
+        // tap is outside the map or t >= T)
+        for (int i = lane; i < taps * DELTA; i += 32) {
+            const int q = i / DELTA, t = i - q * DELTA;
+            const int ci = q / (K * K), r = q - ci * K * K, ky = r / K, kx = r - ky * K;
+            const int iy = y + ky - pad, ix = x + kx - pad;
+            float v = 0.0f;
+            if (iy >= 0 && iy < H && ix >= 0 && ix < W && base + t < T)
+                v = __ldg(frames + ((((n * C_in + ci) * H + iy) * (long long)W + ix) * T) + base + t);
+            s_f[i] = v;
+        }
+        __syncwarp();
+        float in[DELTA][V];
+#pragma unroll
+        for (int t = 0; t < DELTA; ++t)
+#pragma unroll
+            for (int v = 0; v < V; ++v) in[t][v] = 0.0f;
+        for (int q = 0; q < taps; ++q) {
+            const int ci = q / (K * K), r = q - ci * K * K, ky = r / K, kx = r - ky * K;
+            const int iy = y + ky - pad, ix = x + kx - pad;
+            if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;   // warp-uniform
+            float wv[V];
+#pragma unroll
+            for (int v = 0; v < V; ++v)
+                wv[v] = lane_ok ? __ldg(w_oihw + (long long)(c0 + v) * taps + q) : 0.0f;
+#pragma unroll
+            for (int t = 0; t < DELTA; ++t) {
+                const float f = s_f[q * DELTA + t];
+#pragma unroll
+                for (int v = 0; v < V; ++v) in[t][v] = fmaf(wv[v], f, in[t][v]);
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int t = 0; t < DELTA; ++t)
+#pragma unroll
+            for (int v = 0; v < V; ++v) nu.step(base + t, in[t][v], v, cc);
+        if (!__any_sync(FULL_MASK, nu.any())) break;
+    }
+    if (lane_ok) {
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+            out[((n * C_out + c0 + v) * H + y) * (long long)W + x] = nu.res[v];
+    }
+}
+
+// ------------------------------------------------------------------ pool --
+// One thread per output neuron; in[t] = 1 at each of the 4 inputs' spike
+// bins (set, not added).  layout: VDT_LAYOUT_NCHW or VDT_LAYOUT_NHWC.
+__global__ void k_culif_pool(const float* __restrict__ in, float* __restrict__ out, int N, int C, int H_in,
+                             int W_in, int layout, int delta, int NC, float decay, float th) {
+    const int H_out = H_in / 2, W_out = W_in / 2;
+    const long long total = (long long)N * C * H_out * W_out;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+        long long n;
+        int c, yo, xo;
+        if (layout == VDT_LAYOUT_NCHW) {
+            xo = (int)(idx % W_out);
+            yo = (int)((idx / W_out) % H_out);
+            c = (int)((idx / ((long long)W_out * H_out)) % C);
+            n = idx / ((long long)W_out * H_out * C);
+        } else {
+            c = (int)(idx % C);
+            xo = (int)((idx / C) % W_out);
+            yo = (int)((idx / ((long long)C * W_out)) % H_out);
+            n = idx / ((long long)C * W_out * H_out);
+        }
+        float tf[4];
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+            const int yy = yo * 2 + (d >> 1), xx = xo * 2 + (d & 1);
+            const long long at = layout == VDT_LAYOUT_NCHW ? ((n * C + c) * H_in + yy) * (long long)W_in + xx
+                                                            : ((n * H_in + yy) * (long long)W_in + xx) * C + c;
+            tf[d] = __ldg(in + at);
+        }
+        float I = 0.0f, V = 0.0f, res = 9999.0f;
+        for (int tau = 0; tau < NC; ++tau) {
+            const int base = tau * delta;
+            unsigned long long set = 0;                      // bins of this chunk holding a spike
+#pragma unroll
+            for (int d = 0; d < 4; ++d)
+                if (tf[d] >= (float)base && tf[d] < (float)(base + delta)) set |= 1ull << ((int)tf[d] - base);
+            bool fired = false;
+            for (int t = 0; t < delta; ++t) {
+                I = fmaf(I, decay, (set >> t) & 1ull ? 1.0f : 0.0f);
+                V += I;
+                if (V >= th) { res = (float)(base + t); fired = true; break; }
+            }
+            if (fired) break;
+        }
+        out[idx] = res;
+    }
+}
+
+// -------------------------------------------------------------- FC1 (rec) --
+// One CTA per sample, one thread per output neuron (F_out <= 1024).  Per
+// chunk the feed-forward input in_ff[t][i] is summed in shared memory in the
+// reference's order (the sample's bucket, ascending j inside a chunk), then
+// the chunk's steps run in lock-step: the recurrent input of neuron i sums
+// W_rec[i][j] over the neurons j that fired on the previous step (ascending
+// j), I = fma(I, decay, in_ff) + in_rec, V += I; a neuron fires once and
+// its V is reset to -10000.  No early exit.  Weights are transposed:
+// w_t[j][i] = W_fc1[i][j], wrec_t[j][i] = W_rec[i][j].
+__global__ void k_culif_fc1_rec(const int* __restrict__ off, const int* __restrict__ bcin,
+                                const float* __restrict__ btin, const float* __restrict__ w_t,
+                                const float* __restrict__ wrec_t, float* __restrict__ out, int F_in,
+                                int F_out, int delta, int NC, float decay, float th) {
+    extern __shared__ float f1_sm[];
+    float* s_ff = f1_sm;                                     // [delta][F_out]
+    unsigned* s_prev = reinterpret_cast<unsigned*>(s_ff + (size_t)delta * F_out);   // fired bitmap
+    const int i = threadIdx.x;
+    const long long n = blockIdx.x;
+    const int words = (F_out + 31) / 32;
+    for (int k = i; k < words; k += blockDim.x) s_prev[k] = 0u;
+    float I = 0.0f, V = 0.0f, fire = 9999.0f;
+    bool has = false;
+    const int OS = NC + 1;
+    const int* sc = bcin + n * F_in;
+    const float* st = btin + n * F_in;
+    for (int ch = 0; ch < NC; ++ch) {
+        const int base = ch * delta;
+        for (int t = 0; t < delta; ++t) s_ff[t * F_out + i] = 0.0f;
+        const int s = __ldg(off + n * OS + ch), e = __ldg(off + n * OS + ch + 1);
+        for (int p = s; p < e; ++p) {
+            const int j = __ldg(sc + p);
+            const int tt = (int)__ldg(st + p);
+            s_ff[(tt - base) * F_out + i] += __ldg(w_t + (long long)j * F_out + i);
+        }
+        for (int t = 0; t < delta; ++t) {
+            __syncthreads();                                 // previous step's bitmap complete
+            float in_rec = 0.0f;
+            for (int k = 0; k < words; ++k) {
+                unsigned m = s_prev[k];
+                while (m) {
+                    const int b = __ffs(m) - 1;
+                    m &= m - 1;
+                    in_rec += __ldg(wrec_t + (long long)(k * 32 + b) * F_out + i);
+                }
+            }
+            I = fmaf(I, decay, s_ff[t * F_out + i]) + in_rec;
+            V += I;
+            bool now = false;
+            if (V >= th && !has) { now = true; has = true; fire = (float)(base + t); V = -10000.0f; }
+            __syncthreads();                                 // everyone read the old bitmap
+            const unsigned bits = __ballot_sync(FULL_MASK, now);
+            if ((i & 31) == 0) s_prev[i >> 5] = bits;
+        }
+    }
+    out[n * F_out + i] = fire;
+}
+
+// OIHW -> HWIO ([K][K][C_in][C_out]) weight permutation
+__global__ void k_oihw_to_hwio(const float* __restrict__ src, float* __restrict__ dst, int O, int I, int K) {
+    const long long total = (long long)O * I * K * K;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long d = (long long)blockIdx.x * blockDim.x + threadIdx.x; d < total; d += stride) {
+        const int o = (int)(d % O);
+        long long r = d / O;
+        const int ci = (int)(r % I);
+        r /= I;
+        const int kx = (int)(r % K), ky = (int)(r / K);
+        dst[d] = src[(((long long)o * I + ci) * K + ky) * K + kx];
+    }
+}
+
+unsigned grid_1d(long long n, int threads) {
+    long long b = (n + threads - 1) / threads;
+    const long long cap = 148LL * 32;
+    return (unsigned)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+template <int V, int DELTA>
+cudaError_t launch_conv1_vd(const float* frames, const float* w, float* out, int N, int C_in, int C_out, int H,
+                            int W, int K, int T, int NC, float decay, float th, cudaStream_t s) {
+    const size_t smem = (size_t)C1_WARPS * C_in * K * K * DELTA * sizeof(float);
+    auto kern = k_culif_conv1<V, DELTA>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    const long long warps = (long long)N * H * W;
+    kern<<<(unsigned)((warps + C1_WARPS - 1) / C1_WARPS), C1_WARPS * 32, smem, s>>>(
+        frames, w, out, N, C_in, C_out, H, W, K, T, NC, decay, th);
+    return cudaGetLastError();
+}
+
+template <int V>
+cudaError_t launch_conv1_v(const float* frames, const float* w, float* out, int N, int C_in, int C_out, int H,
+                           int W, int K, int T, int delta, float decay, float th, cudaStream_t s) {
+    const int NC = (T + delta - 1) / delta;
+    switch (delta) {
+        case 8: return launch_conv1_vd<V, 8>(frames, w, out, N, C_in, C_out, H, W, K, T, NC, decay, th, s);
+        case 16: return launch_conv1_vd<V, 16>(frames, w, out, N, C_in, C_out, H, W, K, T, NC, decay, th, s);
+        case 32: return launch_conv1_vd<V, 32>(frames, w, out, N, C_in, C_out, H, W, K, T, NC, decay, th, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+bool culif_conv1_supported(int C_in, int C_out, int K, int delta) {
+    if (delta != 8 && delta != 16 && delta != 32) return false;
+    if (C_out > 128 || K > 7) return false;
+    return (size_t)C1_WARPS * C_in * K * K * delta * sizeof(float) <= 200 * 1024;
+}
+
+cudaError_t launch_culif_conv1(const float* frames, const float* w_oihw, float* out, int N, int C_in, int C_out,
+                               int H, int W, int K, int T, int delta, float decay, float th, cudaStream_t s) {
+    if (!culif_conv1_supported(C_in, C_out, K, delta)) return cudaErrorInvalidValue;
+    if (N <= 0) return cudaSuccess;
+    if (C_out <= 32) return launch_conv1_v<1>(frames, w_oihw, out, N, C_in, C_out, H, W, K, T, delta, decay, th, s);
+    if (C_out <= 64) return launch_conv1_v<2>(frames, w_oihw, out, N, C_in, C_out, H, W, K, T, delta, decay, th, s);
+    return launch_conv1_v<4>(frames, w_oihw, out, N, C_in, C_out, H, W, K, T, delta, decay, th, s);
+}
+
+cudaError_t launch_culif_pool(const float* in, float* out, int N, int C, int H_in, int W_in, int layout,
+                              int T, int delta, float decay, float th, cudaStream_t s) {
+    if (delta < 1 || delta > 64) return cudaErrorInvalidValue;
+    const long long total = (long long)N * C * (H_in / 2) * (W_in / 2);
+    if (total <= 0) return cudaSuccess;
+    const int NC = (T + delta - 1) / delta;
+    k_culif_pool<<<grid_1d(total, 256), 256, 0, s>>>(in, out, N, C, H_in, W_in, layout, delta, NC, decay, th);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_culif_fc1_rec(const int* off, const int* cin, const float* tin, const float* w_t,
+                                 const float* wrec_t, float* out, int N, int F_in, int F_out, int T, int delta,
+                                 float decay, float th, cudaStream_t s) {
+    if (F_out < 1 || F_out > 1024 || F_out % 32 != 0 || delta < 1) return cudaErrorInvalidValue;
+    if (N <= 0) return cudaSuccess;
+    const int NC = (T + delta - 1) / delta;
+    const size_t smem = (size_t)delta * F_out * sizeof(float) + (size_t)(F_out / 32) * sizeof(unsigned);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k_culif_fc1_rec, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    k_culif_fc1_rec<<<N, F_out, smem, s>>>(off, cin, tin, w_t, wrec_t, out, F_in, F_out, delta, NC, decay, th);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_oihw_to_hwio(const float* src, float* dst, int O, int I, int K, cudaStream_t s) {
+    const long long total = (long long)O * I * K * K;
+    if (total <= 0) return cudaSuccess;
+    k_oihw_to_hwio<<<grid_1d(total, 256), 256, 0, s>>>(src, dst, O, I, K);
+    return cudaGetLastError();
+}
+
+}  // namespace vdt

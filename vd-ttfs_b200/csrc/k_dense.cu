@@ -25,6 +25,7 @@ namespace vdt {
 namespace {
 
 constexpr int DW = 4;         // warps per CTA
+constexpr int FS = 8;         // weight rows in flight per streamed block
 constexpr int DENSE_WIN = 36; // largest fan-in handled: 36 windows of 32 inputs
 
 // shared words per warp: event records (int2 per input), step bins (T + 1),
@@ -42,11 +43,6 @@ __device__ __forceinline__ int tap_of(int f, int C_in, float inv) {
     else if ((j + 1) * C_in <= f) ++j;
     return j;
 }
-
-// weight rows in flight per streamed block: fewer for the widest fan-ins,
-// whose inputs take more registers during the sort
-template <int R>
-__host__ __device__ constexpr int dense_fs() { return R <= 18 ? 8 : 4; }
 
 template <int V, int R, int MINB, bool COUNT>
 __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const float* __restrict__ in,
@@ -179,7 +175,7 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
     const float* Wl = p.W + (lane_ok ? c0 : 0);
     int next_t = 0;
     if constexpr (!COUNT) {
-        if (stream_runs<V, dense_fs<R>()>(nu, s_list, 0, s_runs, nruns, Wl, next_t, tt))
+        if (stream_runs<V, FS>(nu, s_list, 0, s_runs, nruns, Wl, next_t, tt))
             nu.close_empty(next_t, p.T, tt);
     } else {
         // fetched synapses, reference chunk accounting: chunk c counts its
@@ -227,7 +223,6 @@ cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t 
                         (size_t)(p.decay_len + 2 * p.T) * sizeof(float);
     // register budget tuned for occupancy (the kernel is latency-bound): the
     // streamed block, lane state and the sort's input registers
-    constexpr int FS = dense_fs<R>();
     constexpr int REGS = FS * V + 2 * FS + 4 * V + R;
     constexpr int MINB = (65536 / (DW * 32 * REGS)) > 8 ? 8 : (65536 / (DW * 32 * REGS));
     auto kern = p.fetched ? k_dense<V, R, MINB, true> : k_dense<V, R, MINB, false>;

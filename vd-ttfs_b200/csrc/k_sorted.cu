@@ -22,6 +22,8 @@
 //   The warp stops once all its neurons fired (later chunks are never
 //   fetched).  A chunk with more events than the per-warp record buffer is
 //   integrated in arrival-order segments into per-slot registers instead.
+#include <type_traits>
+
 #include "lanes.h"
 #include "vdt_internal.h"
 
@@ -80,7 +82,8 @@ __device__ __forceinline__ void stream_all(float (&d)[DELTA][V], const int2* rec
     }
 }
 
-template <int DELTA, int V, int MINB>
+// CULIF selects the task-3 neuron (CulifLanes, no LUT, every step scanned)
+template <int DELTA, int V, int MINB, bool CULIF>
 __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int n_warps, int groups) {
     extern __shared__ __align__(16) int sm[];
     __shared__ int s_floor, s_mono;
@@ -102,8 +105,12 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
     float* s_decay = reinterpret_cast<float*>(sm + SWARPS * words);
     float* s_th = s_decay + p.decay_len;
     float* s_thx = s_th + p.T;
-    for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
-    const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
+    ThTables tt{};
+    if constexpr (!CULIF) {
+        for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
+        tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
+    }
+    const CulifCfg cc{p.culif_decay, p.culif_th};
 
     const int gw = blockIdx.x * SWARPS + warp;
     if (gw >= n_warps) return;                               // warp-uniform
@@ -146,8 +153,9 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
     }
     __syncwarp();
 
-    Lanes<V> nu;
-    nu.init(p.bias, c0, lane_ok, p.inf_time);
+    std::conditional_t<CULIF, CulifLanes<V>, Lanes<V>> nu;
+    if constexpr (CULIF) nu.init(lane_ok, p.inf_time);
+    else nu.init(p.bias, c0, lane_ok, p.inf_time);
     unsigned long long fetched = 0;
     const float* Wl = p.W + (lane_ok ? c0 : 0);
     const unsigned lt = (1u << lane) - 1u;
@@ -168,9 +176,18 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
             if (lane >= dd) inc += u;
         }
         const int total = __shfl_sync(FULL_MASK, inc, 31);
-        if (total == 0) continue;                            // closed lazily
-        nu.close_empty(next_t, base, tt);                    // input-free steps before the chunk
-        next_t = base;
+        if constexpr (CULIF) {
+            if (total == 0) {                                // every step still integrates
+                nu.close_empty(next_t, base + DELTA, cc);
+                next_t = base + DELTA;
+                done = !__any_sync(FULL_MASK, nu.any());
+                continue;
+            }
+        } else {
+            if (total == 0) continue;                        // closed lazily
+            nu.close_empty(next_t, base, tt);                // input-free steps before the chunk
+            next_t = base;
+        }
         if (p.fetched) fetched += (unsigned long long)total * nu.live();
         if (!__any_sync(FULL_MASK, nu.any())) break;
         if (lane < ntaps) { s_pre[lane] = inc - cnt; s_st[lane] = st; }
@@ -201,17 +218,24 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
                     const long long at = s_cbase[lo] + s_st[lo] + (pidx - s_pre[lo]);
                     const int ci = __ldg(p.cin + at);
                     const float t = __ldg(p.tin + at);
-                    int tb = (int)floorf(t - p.tfs);
-                    if (tb < 0) tb = 0;
-                    int ti;
-                    if (p.lut_mode == VDT_LUT_BY_TB) {
-                        ti = tb;
+                    float lv = 1.0f;                         // CuLIF: in[t] += w exactly
+                    int tb;
+                    if constexpr (CULIF) {
+                        tb = (int)t;
                     } else {
-                        ti = (int)t;
-                        ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+                        tb = (int)floorf(t - p.tfs);
+                        if (tb < 0) tb = 0;
+                        int ti;
+                        if (p.lut_mode == VDT_LUT_BY_TB) {
+                            ti = tb;
+                        } else {
+                            ti = (int)t;
+                            ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+                        }
+                        lv = s_decay[ti];
                     }
                     slot = tb - base;
-                    s_tmp[q] = make_int2((s_wrow[lo] + ci) | (slot << 24), __float_as_int(s_decay[ti]));
+                    s_tmp[q] = make_int2((s_wrow[lo] + ci) | (slot << 24), __float_as_int(lv));
                 }
                 const unsigned g = __match_any_sync(FULL_MASK, slot);
                 if (slot >= 0 && lane == __ffs(g) - 1) s_cnt[slot] += __popc(g);
@@ -254,7 +278,8 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
             if (fits) {
                 // 3. the chunk's non-empty slots as runs, then one streamed pass
                 const int nruns = compact_runs(s_start + 1, DELTA, base, s_runs);
-                done = !stream_runs<V, FS>(nu, s_rec, 0, s_runs, nruns, Wl, next_t, tt);
+                if constexpr (CULIF) done = !stream_runs<V, FS>(nu, s_rec, 0, s_runs, nruns, Wl, next_t, cc);
+                else done = !stream_runs<V, FS>(nu, s_rec, 0, s_runs, nruns, Wl, next_t, tt);
             } else {
                 stream_all<DELTA, V>(d, s_rec, s_start, Wl, p.C_out);
             }
@@ -262,20 +287,39 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
         }
         if (!fits) {
             // per-slot chains complete: close the chunk's steps in order
+            // (the CuLIF scan has no t < T guard, t3:137-141)
 #pragma unroll
             for (int i = 0; i < DELTA; ++i) {
-                if (base + i < p.T) {
+                if (CULIF || base + i < p.T) {
 #pragma unroll
                     for (int v = 0; v < V; ++v) nu.acc[v] = d[i][v];
-                    nu.close_step(base + i, tt);
+                    if constexpr (CULIF) nu.close_step_bf(base + i, cc);
+                    else nu.close_step(base + i, tt);
                 }
             }
-            next_t = min(p.T, base + DELTA);
+            next_t = CULIF ? base + DELTA : min(p.T, base + DELTA);
             done = !__any_sync(FULL_MASK, nu.any());
+        } else if constexpr (CULIF) {
+            if (!done) {
+                nu.close_empty(next_t, base + DELTA, cc);    // the chunk's remaining steps
+                next_t = base + DELTA;
+                done = !__any_sync(FULL_MASK, nu.any());
+            }
         }
     }
-    if (!done) nu.close_empty(next_t, p.T, tt);
-    if (lane_ok) store_res<V>(p.out + (long long)pix * p.C_out + c0, nu.res);
+    if constexpr (!CULIF) {
+        if (!done) nu.close_empty(next_t, p.T, tt);
+    }
+    if (lane_ok) {
+        if (p.out_nchw) {
+            const long long plane = (long long)p.H_out * p.W_out;
+            const long long site = (long long)h_out * p.W_out + w_out;
+#pragma unroll
+            for (int v = 0; v < V; ++v) p.out[(img * p.C_out + c0 + v) * plane + site] = nu.res[v];
+        } else {
+            store_res<V>(p.out + (long long)pix * p.C_out + c0, nu.res);
+        }
+    }
     if (p.fetched) {
 #pragma unroll
         for (int dd = 16; dd > 0; dd >>= 1) fetched += __shfl_down_sync(FULL_MASK, fetched, dd);
@@ -289,16 +333,16 @@ int pick_v_sorted(int C_out, int delta) {
     return 1;
 }
 
-template <int DELTA, int V>
+template <int DELTA, int V, bool CULIF>
 cudaError_t launch_sorted_dv(const IntegParams& p, cudaStream_t s, int n_warps, int groups) {
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
     const size_t smem = (size_t)SWARPS * sorted_words(ntaps, p.NC + 1) * sizeof(int) +
-                        (size_t)(p.decay_len + 2 * p.T) * sizeof(float);
+                        (CULIF ? 0 : (size_t)(p.decay_len + 2 * p.T) * sizeof(float));
     // registers: the streamed block (FS weight rows + records) plus lane
     // state; the rare oversize-chunk path may spill
     constexpr int REGS = FS * V + 2 * FS + 4 * V + 60;
     constexpr int MINB = (65536 / (SWARPS * 32 * REGS)) > 8 ? 8 : (65536 / (SWARPS * 32 * REGS));
-    auto kern = k_sorted<DELTA, V, MINB>;
+    auto kern = k_sorted<DELTA, V, MINB, CULIF>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
@@ -307,7 +351,7 @@ cudaError_t launch_sorted_dv(const IntegParams& p, cudaStream_t s, int n_warps, 
     return cudaGetLastError();
 }
 
-template <int DELTA>
+template <int DELTA, bool CULIF>
 cudaError_t launch_sorted_d(const IntegParams& p, cudaStream_t s) {
     const int V = pick_v_sorted(p.C_out, DELTA);
     const int groups = (p.C_out + 32 * V - 1) / (32 * V);
@@ -317,9 +361,23 @@ cudaError_t launch_sorted_d(const IntegParams& p, cudaStream_t s) {
     if (n_warps >= (1ll << 31)) return cudaErrorInvalidValue;   // 32-bit work index
     const int nw = (int)n_warps;
     switch (V) {
-        case 4: return launch_sorted_dv<DELTA, (DELTA <= 8 ? 4 : 1)>(p, s, nw, groups);
-        case 2: return launch_sorted_dv<DELTA, (DELTA <= 16 ? 2 : 1)>(p, s, nw, groups);
-        default: return launch_sorted_dv<DELTA, 1>(p, s, nw, groups);
+        case 4: return launch_sorted_dv<DELTA, (DELTA <= 8 ? 4 : 1), CULIF>(p, s, nw, groups);
+        case 2: return launch_sorted_dv<DELTA, (DELTA <= 16 ? 2 : 1), CULIF>(p, s, nw, groups);
+        default: return launch_sorted_dv<DELTA, 1, CULIF>(p, s, nw, groups);
+    }
+}
+
+template <bool CULIF>
+cudaError_t launch_sorted_any(const IntegParams& p, cudaStream_t s) {
+    switch (p.delta) {
+        case 1: return launch_sorted_d<1, CULIF>(p, s);
+        case 2: return launch_sorted_d<2, CULIF>(p, s);
+        case 4: return launch_sorted_d<4, CULIF>(p, s);
+        case 8: return launch_sorted_d<8, CULIF>(p, s);
+        case 16: return launch_sorted_d<16, CULIF>(p, s);
+        case 32: return launch_sorted_d<32, CULIF>(p, s);
+        case 64: return launch_sorted_d<64, CULIF>(p, s);
+        default: return cudaErrorInvalidValue;
     }
 }
 
@@ -337,17 +395,12 @@ bool sorted_supported(int K, int is_fc, int delta, int C_in, int C_out, int T, i
            200 * 1024;
 }
 
-cudaError_t launch_sorted(const IntegParams& p, cudaStream_t s) {
-    switch (p.delta) {
-        case 1: return launch_sorted_d<1>(p, s);
-        case 2: return launch_sorted_d<2>(p, s);
-        case 4: return launch_sorted_d<4>(p, s);
-        case 8: return launch_sorted_d<8>(p, s);
-        case 16: return launch_sorted_d<16>(p, s);
-        case 32: return launch_sorted_d<32>(p, s);
-        case 64: return launch_sorted_d<64>(p, s);
-        default: return cudaErrorInvalidValue;
-    }
+cudaError_t launch_sorted(const IntegParams& p, cudaStream_t s) { return launch_sorted_any<false>(p, s); }
+
+bool culif_supported(int K, int is_fc, int delta, int C_in, int C_out, int T) {
+    return sorted_supported(K, is_fc, delta, C_in, C_out, T, 0);
 }
+
+cudaError_t launch_culif(const IntegParams& p, cudaStream_t s) { return launch_sorted_any<true>(p, s); }
 
 }  // namespace vdt

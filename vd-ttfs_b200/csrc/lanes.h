@@ -159,6 +159,65 @@ struct Lanes {
     }
 };
 
+// CuLIF neurons of task 3 (conv_bucketed_early t3:109-143, fc2_bucketed_early
+// t3:203-225): every step t updates I = fma(I, decay, in[t]); V += I and the
+// neuron fires at the first t with V >= th.  A step without input has
+// in[t] = 0, so no step can be skipped.
+struct CulifCfg {
+    float decay, th;
+};
+
+template <int V>
+struct CulifLanes {
+    float I[V], Vm[V], res[V], acc[V];
+    bool alive[V];
+
+    __device__ __forceinline__ void init(bool lane_ok, float inf_time) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            I[v] = 0.0f;
+            Vm[v] = 0.0f;
+            res[v] = inf_time;
+            acc[v] = 0.0f;
+            alive[v] = lane_ok;
+        }
+    }
+    __device__ __forceinline__ bool any() const {
+        bool a = false;
+#pragma unroll
+        for (int v = 0; v < V; ++v) a |= alive[v];
+        return a;
+    }
+    __device__ __forceinline__ int live() const {
+        int n = 0;
+#pragma unroll
+        for (int v = 0; v < V; ++v) n += alive[v] ? 1 : 0;
+        return n;
+    }
+    __device__ __forceinline__ void step(int s, float in, int v, const CulifCfg& c) {
+        I[v] = fmaf(I[v], c.decay, in);
+        Vm[v] += I[v];
+        const bool fire = alive[v] && Vm[v] >= c.th;
+        res[v] = fire ? (float)s : res[v];
+        alive[v] = alive[v] && !fire;
+    }
+    // step s with input acc (the step's in[] sum), then acc = 0
+    __device__ __forceinline__ void close_step_bf(int s, const CulifCfg& c) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            step(s, acc[v], v, c);
+            acc[v] = 0.0f;
+        }
+    }
+    // steps [a, b) without input
+    __device__ __forceinline__ void close_empty(int a, int b, const CulifCfg& c) {
+        for (int t = a; t < b; ++t) {
+#pragma unroll
+            for (int v = 0; v < V; ++v) step(t, 0.0f, v, c);
+        }
+    }
+};
+
 template <int V>
 __device__ __forceinline__ void load_row(const float* p, float (&w)[V]);
 
@@ -208,8 +267,8 @@ __device__ __forceinline__ void stream_block(Lanes<V>& nu, const int2* rec, cons
 }
 
 // the same from a 32-bit shared address (no generic-pointer arithmetic)
-template <int V, int U>
-__device__ __forceinline__ void stream_block_sa(Lanes<V>& nu, unsigned sa, const float* Wl) {
+template <int V, int U, class L>
+__device__ __forceinline__ void stream_block_sa(L& nu, unsigned sa, const float* Wl) {
     int2 e[U];
     float w[U][V];
 #pragma unroll
@@ -226,10 +285,11 @@ __device__ __forceinline__ void stream_block_sa(Lanes<V>& nu, unsigned sa, const
 // a run's tail is split into blocks of 4, 2 and 1.  Each run ends with the
 // close of its step (input-free steps before it are closed first).  Returns
 // false once every neuron of the warp has fired (the caller may stop).
-template <int V, int FS>
-__device__ __forceinline__ bool stream_runs(Lanes<V>& nu, const int2* rec, int k, const int2* runs,
+template <int V, int FS, class L, class TT>
+__device__ __forceinline__ bool stream_runs(L& nu, const int2* rec, int k, const int2* runs,
                                             int nruns, const float* Wl, int& next_t,
-                                            const ThTables& tt) {
+                                            const TT& tt) {
+    static_assert(FS == 4 || FS == 8, "a run's tail is covered by blocks of 4, 2 and 1");
     const unsigned sa0 = (unsigned)__cvta_generic_to_shared(rec);
     for (int j = 0; j < nruns; ++j) {
         const int2 rn = runs[j];

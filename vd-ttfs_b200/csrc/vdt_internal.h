@@ -47,6 +47,10 @@ struct IntegParams {
     int T, delta, NC, t_min, lut_mode, decay_len;
     float tfs, inf_time;
     unsigned long long* fetched;  // optional synapse counter (may be null)
+    // task-3 CuLIF layers (launch_culif): constant current decay and threshold;
+    // out_nchw = 1 writes the output map NCHW [B, C_out, H_out, W_out]
+    float culif_decay, culif_th;
+    int out_nchw;
 };
 cudaError_t launch_integrate(const IntegParams& p, cudaStream_t s);
 // true when launch_integrate supports this (K, delta, C_out) combination
@@ -62,6 +66,23 @@ bool dense_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len
 cudaError_t launch_sorted(const IntegParams& p, cudaStream_t s);
 // chunk width the runtime buckets k_sorted layers at (outside counting passes)
 constexpr int kSortedDelta = 8;
+
+// Task-3 bucketed CuLIF layer (conv_bucketed_early t3:109-143 with K = 3,
+// fc2_bucketed_early t3:203-225 with is_fc): k_sorted's event path with the
+// CuLIF step; buckets by tb = (int)t (VDT_TB_TRUNC), weights HWIO / [in, out].
+cudaError_t launch_culif(const IntegParams& p, cudaStream_t s);
+bool culif_supported(int K, int is_fc, int delta, int C_in, int C_out, int T);
+
+// Task-3 layers that are not bucketed integrators (k_culif.cu)
+bool culif_conv1_supported(int C_in, int C_out, int K, int delta);
+cudaError_t launch_culif_conv1(const float* frames, const float* w_oihw, float* out, int N, int C_in, int C_out,
+                               int H, int W, int K, int T, int delta, float decay, float th, cudaStream_t s);
+cudaError_t launch_culif_pool(const float* in, float* out, int N, int C, int H_in, int W_in, int layout,
+                              int T, int delta, float decay, float th, cudaStream_t s);
+cudaError_t launch_culif_fc1_rec(const int* off, const int* cin, const float* tin, const float* w_t,
+                                 const float* wrec_t, float* out, int N, int F_in, int F_out, int T, int delta,
+                                 float decay, float th, cudaStream_t s);
+cudaError_t launch_oihw_to_hwio(const float* src, float* dst, int O, int I, int K, cudaStream_t s);
 bool sorted_supported(int K, int is_fc, int delta, int C_in, int C_out, int T, int decay_len);
 
 // -------------------------------------------------------------- edges / LUT

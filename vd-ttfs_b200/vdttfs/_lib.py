@@ -74,6 +74,13 @@ SIGNATURES = {
     "vdt_readout": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_float, _vp, _vp]),
     "vdt_ctx_layer_kernels": (C.c_int, [_vp, C.c_int, _vp]),
     "vdt_ctx_set_layer_kernel": (C.c_int, [_vp, C.c_int, C.c_int]),
+    "vdt_dvs_conv1_raw": (C.c_int, [_vp, _vp] + [C.c_int] * 8 + [C.c_float, C.c_float, _vp, _vp]),
+    "vdt_dvs_conv_bucketed": (C.c_int, [_vp, _vp, _vp, _vp] + [C.c_int] * 8 +
+                              [C.c_float, C.c_float, C.c_int, _vp, _vp]),
+    "vdt_dvs_pool": (C.c_int, [_vp, _vp] + [C.c_int] * 7 + [C.c_float, C.c_float, _vp]),
+    "vdt_dvs_fc1_recurrent": (C.c_int, [_vp] * 5 + [C.c_int] * 5 + [C.c_float, C.c_float, _vp, _vp]),
+    "vdt_dvs_fc2": (C.c_int, [_vp] * 4 + [C.c_int] * 5 + [C.c_float, C.c_float, _vp, _vp]),
+    "vdt_oihw_to_hwio": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, _vp]),
     "vdt_noalloc_scratch_bytes": (C.c_size_t, []),
     "vdt_conv_layer_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, C.c_int, C.c_int,
                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,

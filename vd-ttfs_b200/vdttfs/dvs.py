@@ -1,0 +1,145 @@
+"""Task 3 (DVS gesture) on the engine: the reference's CuLIF stages
+(task3_dvsgesture/vdttfs_cuda/snn_inference_timesorted.cu, "t3") as device
+calls through the C ABI, and the per-batch pipeline of its main.
+
+  conv1_raw        conv1_raw_early        t3:30-65
+  bucketize        k_bucketize_conv/fc    t3:70-106   (VDT_TB_TRUNC)
+  conv_bucketed    conv_bucketed_early    t3:109-143
+  pool             pool_chunk_early       t3:146-168
+  fc1_recurrent    fc1_bucketed_recurrent t3:171-200
+  fc2              fc2_bucketed_early     t3:203-225
+  readout          argmin, lowest index   t3:295-296
+
+Maps are NCHW fp32 spike times as in the reference.  Weights arrive in the
+reference's layouts (OIHW convs, [out, in] FC, [hidden, hidden] recurrent)
+and are permuted once on the device (DvsWeights).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import nets
+from ._lib import TimeCfg, check, lib
+from .engine import LAYOUT_NCHW, LAYOUT_NHWC, TB_TRUNC, _ptr, _stream, bucketize, readout
+
+
+def _cfg(spec: nets.DvsSpec) -> TimeCfg:
+    return TimeCfg(spec.T, spec.delta, 0.0, 1.0, 9999.0, nets.LUT_BY_TB, spec.T, 0)
+
+
+class DvsWeights:
+    """Device copies of a DVS network's weights in the kernels' layouts."""
+
+    def __init__(self, spec: nets.DvsSpec, wts: dict, device="cuda"):
+        import torch
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(device)
+        self.spec = spec
+        self.conv1 = t(wts["conv1"])                           # OIHW, read as is
+        self.conv2 = oihw_to_hwio(t(wts["conv2"]))
+        self.conv3 = oihw_to_hwio(t(wts["conv3"]))
+        self.fc1_t = t(np.asarray(wts["fc1"]).T)                # [F_in, hidden]
+        self.rec_t = t(np.asarray(wts["fc1_rec"]).T)            # [hidden, hidden], [j][i]
+        self.fc2_t = t(np.asarray(wts["fc2"]).T)                # [hidden, classes]
+
+
+def oihw_to_hwio(w, stream=None):
+    import torch
+    O, I, K, _ = w.shape
+    out = torch.empty((K, K, I, O), dtype=torch.float32, device=w.device)
+    check(lib().vdt_oihw_to_hwio(_ptr(w), _ptr(out), O, I, K, C.c_void_p(_stream(stream))), "vdt_oihw_to_hwio")
+    return out
+
+
+def conv1_raw(frames, w_oihw, spec: nets.DvsSpec, stream=None):
+    import torch
+    N = frames.shape[0]
+    c1 = spec.convs[0]
+    out = torch.empty((N, c1, spec.H, spec.W), dtype=torch.float32, device=frames.device)
+    check(lib().vdt_dvs_conv1_raw(_ptr(frames), _ptr(w_oihw), N, spec.in_c, c1, spec.H, spec.W, spec.k,
+                                  spec.T, spec.delta, spec.decay_conv, spec.th_conv, _ptr(out),
+                                  C.c_void_p(_stream(stream))), "vdt_dvs_conv1_raw")
+    return out
+
+
+def bucketize_sites(x, N, C_in, H, W, spec, stream=None):
+    """Buckets of an NCHW map, one column per site (k_bucketize_conv)."""
+    return bucketize(x.reshape(-1), N * H * W, C_in, _cfg(spec), layout=LAYOUT_NCHW, hw=H * W,
+                     tb_mode=TB_TRUNC, stream=stream)
+
+
+def bucketize_rows(x, N, F, spec, stream=None):
+    """Buckets of [N, F] feature rows (k_bucketize_fc)."""
+    return bucketize(x.reshape(-1), N, F, _cfg(spec), layout=LAYOUT_NHWC, hw=1, tb_mode=TB_TRUNC,
+                     stream=stream)
+
+
+def conv_bucketed(buckets, w_hwio, N, C_in, C_out, H, W, spec, out_layout=LAYOUT_NCHW, stream=None):
+    import torch
+    off, cin, tin = buckets
+    out = torch.empty((N * C_out * H * W,), dtype=torch.float32, device=off.device)
+    check(lib().vdt_dvs_conv_bucketed(_ptr(off), _ptr(cin), _ptr(tin), _ptr(w_hwio), N, C_in, C_out, H, W,
+                                      spec.k, spec.T, spec.delta, spec.decay_conv, spec.th_conv, out_layout,
+                                      _ptr(out), C.c_void_p(_stream(stream))), "vdt_dvs_conv_bucketed")
+    return out
+
+
+def pool(x, N, Cc, H, W, spec, layout=LAYOUT_NCHW, stream=None):
+    import torch
+    out = torch.empty((N * Cc * (H // 2) * (W // 2),), dtype=torch.float32, device=x.device)
+    check(lib().vdt_dvs_pool(_ptr(x), _ptr(out), N, Cc, H, W, layout, spec.T, spec.delta, spec.decay_conv,
+                             spec.th_conv, C.c_void_p(_stream(stream))), "vdt_dvs_pool")
+    return out
+
+
+def fc1_recurrent(buckets, w_t, rec_t, N, F_in, F_out, spec, stream=None):
+    import torch
+    off, cin, tin = buckets
+    out = torch.empty((N * F_out,), dtype=torch.float32, device=off.device)
+    check(lib().vdt_dvs_fc1_recurrent(_ptr(off), _ptr(cin), _ptr(tin), _ptr(w_t), _ptr(rec_t), N, F_in, F_out,
+                                      spec.T, spec.delta, spec.decay_fc, spec.th_fc, _ptr(out),
+                                      C.c_void_p(_stream(stream))), "vdt_dvs_fc1_recurrent")
+    return out
+
+
+def fc2(buckets, w_t, N, F_in, F_out, spec, stream=None):
+    import torch
+    off, cin, tin = buckets
+    out = torch.empty((N * F_out,), dtype=torch.float32, device=off.device)
+    check(lib().vdt_dvs_fc2(_ptr(off), _ptr(cin), _ptr(tin), _ptr(w_t), N, F_in, F_out, spec.T, spec.delta,
+                            spec.decay_fc, spec.th_fc, _ptr(out), C.c_void_p(_stream(stream))), "vdt_dvs_fc2")
+    return out
+
+
+def run(spec: nets.DvsSpec, w: DvsWeights, frames, keep=False, stream=None):
+    """The reference main's per-batch sequence (t3:262-296) on the device:
+    frames [N, C_in, H, W, T] -> maps, outputs [N, classes], predictions."""
+    N = frames.shape[0]
+    s = spec.stage_shapes()
+    c1n, c2n, c3n = spec.convs
+    H, W = spec.H, spec.W
+    maps = []
+    x = conv1_raw(frames, w.conv1, spec, stream)
+    maps.append(x)
+    x = conv_bucketed(bucketize_sites(x, N, c1n, H, W, spec, stream), w.conv2, N, c1n, c2n, H, W, spec,
+                      stream=stream)
+    maps.append(x)
+    x = pool(x, N, c2n, H, W, spec, stream=stream)
+    maps.append(x)
+    H2, W2 = H // 2, W // 2
+    x = conv_bucketed(bucketize_sites(x, N, c2n, H2, W2, spec, stream), w.conv3, N, c2n, c3n, H2, W2, spec,
+                      stream=stream)
+    maps.append(x)
+    x = pool(x, N, c3n, H2, W2, spec, stream=stream)
+    maps.append(x)
+    x = fc1_recurrent(bucketize_rows(x, N, s["fc1_in"], spec, stream), w.fc1_t, w.rec_t, N, s["fc1_in"],
+                      spec.hidden, spec, stream)
+    maps.append(x)
+    x = fc2(bucketize_rows(x, N, spec.hidden, spec, stream), w.fc2_t, N, spec.hidden, spec.classes, spec, stream)
+    maps.append(x)
+    pred = readout(x, N, spec.classes, nets.READ_ARGMIN_LOWEST, stream=stream)
+    res = {"out": x.reshape(N, spec.classes), "pred": pred}
+    if keep:
+        res["maps"] = maps
+    return res
