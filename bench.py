@@ -41,6 +41,7 @@ CONFIGS = {
     "vgg16": ("vgg16", 3, 256, 0.0, "weak"),
     "lenet5": ("lenet5", 2, 65536, 0.8, "strong"),
     "lenet5_b1024": ("lenet5", 1, 1024, 0.8, "weak"),
+    "dvs": ("dvs", 4, 64, 0.0, "weak"),     # task-3 CuLIF network, 2x128x128 event frames
 }
 
 
@@ -419,11 +420,239 @@ def run_reference(a):
             "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ------------------------------------------------------------ DVS (task 3) --
+def dvs_stages(dvs, spec, w, x, N, marks=None):
+    """The DVS pipeline stage by stage; with `marks`, a CUDA event pair
+    brackets every stage.  Returns (outputs, predictions, event counts)."""
+    import torch
+    s = spec.stage_shapes()
+    c1n, c2n, c3n = spec.convs
+    H, W, H2, W2 = spec.H, spec.W, spec.H // 2, spec.W // 2
+    ev = {}
+
+    def mark(name, fn):
+        if marks is None:
+            return fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = fn()
+        e1.record()
+        marks.append((name, e0, e1))
+        return r
+
+    y = mark("conv1_raw", lambda: dvs.conv1_raw(x, w.conv1, spec))
+    b = mark("bucketize", lambda: dvs.bucketize_sites(y, N, c1n, H, W, spec))
+    ev["conv2"] = b
+    y = mark("conv2", lambda: dvs.conv_bucketed(b, w.conv2, N, c1n, c2n, H, W, spec))
+    y = mark("pool1", lambda: dvs.pool(y, N, c2n, H, W, spec))
+    b = mark("bucketize", lambda: dvs.bucketize_sites(y, N, c2n, H2, W2, spec))
+    ev["conv3"] = b
+    y = mark("conv3", lambda: dvs.conv_bucketed(b, w.conv3, N, c2n, c3n, H2, W2, spec))
+    y = mark("pool2", lambda: dvs.pool(y, N, c3n, H2, W2, spec))
+    b = mark("bucketize", lambda: dvs.bucketize_rows(y, N, s["fc1_in"], spec))
+    ev["fc1"] = b
+    y = mark("fc1", lambda: dvs.fc1_recurrent(b, w.fc1_t, w.rec_t, N, s["fc1_in"], spec.hidden, spec))
+    b = mark("bucketize", lambda: dvs.bucketize_rows(y, N, spec.hidden, spec))
+    ev["fc2"] = b
+    y = mark("fc2", lambda: dvs.fc2(b, w.fc2_t, N, spec.hidden, spec.classes, spec))
+    from vdttfs import engine as E, nets
+    pred = mark("readout", lambda: E.readout(y, N, spec.classes, nets.READ_ARGMIN_LOWEST))
+    return y, pred, ev
+
+
+def dvs_bytes(spec, N, ev):
+    """Algorithmic bytes of one DVS batch: every stage's input map read and
+    output map written once (conv1: the dense frames), the bucketed stages'
+    lists written and read back (8 B per kept event, 4 B per chunk offset),
+    the weights once."""
+    s = spec.stage_shapes()
+    c1n, c2n, c3n = spec.convs
+    HW, HW2, HW4 = spec.H * spec.W, spec.H * spec.W // 4, spec.H * spec.W // 16
+    OS = spec.n_chunks + 1
+    k2 = spec.k * spec.k
+    lists = lambda name, cols: 2 * (8 * int(ev[name][0][:, -1].sum().item()) + 4 * cols * OS)
+    b = 4 * N * spec.in_c * HW * spec.T + 4 * N * c1n * HW + 4 * c1n * spec.in_c * k2          # conv1
+    b += 4 * N * c1n * HW + 4 * N * c2n * HW + lists("conv2", N * HW) + 4 * c2n * c1n * k2    # conv2
+    b += 4 * N * c2n * HW + 4 * N * c2n * HW2                                                    # pool1
+    b += 4 * N * c2n * HW2 + 4 * N * c3n * HW2 + lists("conv3", N * HW2) + 4 * c3n * c2n * k2  # conv3
+    b += 4 * N * c3n * HW2 + 4 * N * c3n * HW4                                                   # pool2
+    b += 4 * N * s["fc1_in"] + 4 * N * spec.hidden + lists("fc1", N) + 4 * s["fc1_in"] * spec.hidden \
+        + 4 * spec.hidden * spec.hidden                                                         # fc1
+    b += 4 * N * spec.hidden + 4 * N * spec.classes + lists("fc2", N) + 4 * spec.hidden * spec.classes
+    return b
+
+
+def run_dvs_engine(a):
+    import torch
+    import torch.distributed as dist
+    from vdttfs import dvs, nets, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    _, cfg_id, Bcfg, _, scaling = CONFIGS["dvs"]
+    B = a.batch or Bcfg
+    spec = nets.dvs()
+    wts = synth.dvs_weights(spec, cfg_id)
+    w = dvs.DvsWeights(spec, wts, dev)
+    frames = synth.dvs_frames(cfg_id, B, spec, stream=rank)
+    x_dev = torch.from_numpy(frames).to(dev)
+    gathered = torch.empty((world * B,), dtype=torch.int32, device=dev) if world > 1 else None
+    stream = torch.cuda.current_stream(dev)
+
+    def step(x):
+        _, pred, _ = dvs_stages(dvs, spec, w, x, B)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, pred)
+        return pred
+
+    for _ in range(a.warmup):
+        step(x_dev)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local, enabled=(rank == 0 and not a.no_clocks))
+    clocks.start()
+    times = []
+    for _ in range(a.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step(x_dev)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    clk = clocks.stop()
+    tot_ms = float(np.sum(times))
+    if world > 1:
+        t = torch.tensor([tot_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tot_ms = float(t.item())
+    value = world * B * a.steps / (tot_ms / 1e3)
+
+    # end to end: pinned host frames -> device, the network, outputs back
+    h_in = torch.from_numpy(frames).pin_memory()
+    h_out = torch.empty((B, spec.classes), dtype=torch.float32).pin_memory()
+    h_pred = torch.empty((B,), dtype=torch.int32).pin_memory()
+    x_e2e = torch.empty_like(x_dev)
+    e_times = []
+    for it in range(a.steps + 1):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        x_e2e.copy_(h_in, non_blocking=True)
+        y, pred, _ = dvs_stages(dvs, spec, w, x_e2e, B)
+        h_out.copy_(y.reshape(B, spec.classes), non_blocking=True)
+        h_pred.copy_(pred, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if it > 0:                                           # the first pass warms the copies
+            e_times.append(e0.elapsed_time(e1))
+    e_ms = float(np.sum(e_times))
+    if world > 1:
+        t = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e = world * B * a.steps / (e_ms / 1e3)
+
+    # per-stage roofline pass
+    marks = []
+    _, _, ev = dvs_stages(dvs, spec, w, x_dev, B, marks=marks)
+    torch.cuda.synchronize()
+    stage_ms = {}
+    for name, e0, e1 in marks:
+        stage_ms[name] = stage_ms.get(name, 0.0) + e0.elapsed_time(e1)
+    alg = dvs_bytes(spec, B, ev)
+    kern_ms = float(sum(stage_ms.values()))
+    peak, peak_kind = peaks()
+    achieved = alg / (kern_ms / 1e3) / 1e9
+    conv1_bytes = 4 * B * spec.in_c * spec.H * spec.W * spec.T + 4 * B * spec.convs[0] * spec.H * spec.W
+    res = None
+    if rank == 0:
+        res = {
+            "metric": "images_per_sec", "value": round(value, 1), "unit": "samples/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(tot_ms / a.steps, 4), "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded Bernoulli(0.05) event frames, Kaiming weights, see vdttfs/synth.py)",
+            "config": {"workload": f"dvs C{cfg_id}", "model": "dvs-culif 2x128x128, 11 classes",
+                       "global_batch": world * B, "batch_per_gpu": B, "T": spec.T, "delta": spec.delta,
+                       "parallelism": f"dp{world}", "l2": "inputs larger than L2 (frames 21 MB per sample)"},
+            "e2e": {"value": round(e2e, 1), "unit": "samples/s", "h2d_bytes_per_step": int(frames.nbytes),
+                    "d2h_bytes_per_step": int(B * spec.classes * 4 + B * 4)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "kernel": "all DVS stages of one step", "peak_source": f"{peak_kind} hbm_gbs",
+                         "algorithmic_bytes_per_step": int(alg), "kernel_ms_per_step": round(kern_ms, 4),
+                         "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+                         "conv1_gbs": round(conv1_bytes / (stage_ms["conv1_raw"] / 1e3) / 1e9, 1)},
+            "gpu_launches": 13 * a.steps,
+            "clocks": clk,
+        }
+        if not a.no_cpu_baseline:
+            res["cpu_baseline"] = dvs_cpu_baseline(spec, wts, frames, budget_s=20.0)
+    if world > 1:
+        dist.destroy_process_group()
+    return res
+
+
+def dvs_cpu_baseline(spec, wts, frames, budget_s=20.0):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cores = os.cpu_count() or 1
+    n, reps, t_tot = 1, 0, 0.0
+    while t_tot < budget_s * 0.5 and reps < 8:
+        t0 = time.perf_counter()
+        O.run_dvs(spec, wts, frames[:n])
+        t_tot += time.perf_counter() - t0
+        reps += 1
+    return {"value": round(n * reps / t_tot, 3), "unit": "samples/s", "cores": cores, "kind": "port",
+            "sample": f"{reps} passes of {n} sample of the same workload (full DVS network), "
+                      f"OpenMP over {cores} threads"}
+
+
+def run_dvs_reference(a):
+    from vdttfs import nets, synth
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    _, cfg_id, _, _, scaling = CONFIGS["dvs"]
+    spec = nets.dvs()
+    wts = synth.dvs_weights(spec, cfg_id)
+    n = 1
+    frames = synth.dvs_frames(cfg_id, n, spec, stream=0)
+    for _ in range(a.warmup):
+        O.run_dvs(spec, wts, frames)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        O.run_dvs(spec, wts, frames)
+    dt = time.perf_counter() - t0
+    cores = os.cpu_count() or 1
+    v = round(n * a.steps / dt, 3)
+    return {"impl": "reference", "metric": "images_per_sec", "value": v, "unit": "samples/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt / a.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": f"dvs C{cfg_id}", "batch_per_step": n, "T": spec.T, "delta": spec.delta},
+            "cpu_baseline": {"value": v, "unit": "samples/s", "cores": cores, "kind": "port",
+                             "sample": f"{n} sample per step, the CPU port of the reference's task-3 "
+                                       f"path (oracle/vdt_oracle.c), OpenMP {cores} threads"},
+            "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def main():
     a = parse()
     if a.warmup < 3:
         a.warmup = 3
-    res = run_reference(a) if a.impl == "reference" else run_engine(a)
+    if a.config == "dvs":
+        res = run_dvs_reference(a) if a.impl == "reference" else run_dvs_engine(a)
+    else:
+        res = run_reference(a) if a.impl == "reference" else run_engine(a)
     if res is not None:
         print(json.dumps(res), flush=True)
 
