@@ -440,7 +440,8 @@ def dvs_stages(dvs, spec, w, x, N, marks=None):
         marks.append((name, e0, e1))
         return r
 
-    y = mark("conv1_raw", lambda: dvs.conv1_raw(x, w.conv1, spec))
+    spec0, spec = spec, dvs.internal_spec(spec)
+    y = mark("conv1_raw", lambda: dvs.conv1_raw(x, w.conv1, spec0))
     b = mark("bucketize", lambda: dvs.bucketize_sites(y, N, c1n, H, W, spec))
     ev["conv2"] = b
     y = mark("conv2", lambda: dvs.conv_bucketed(b, w.conv2, N, c1n, c2n, H, W, spec))

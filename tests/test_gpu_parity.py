@@ -65,6 +65,21 @@ def test_bucketize_nhwc_bitexact(O, dev, c_in, T, delta, tfs):
     bucket_valid_equal(_np(off), _np(cin), _np(tin), roff, rcin, rtin)
 
 
+@pytest.mark.parametrize("n_cols,c_in,T,delta,tb_mode", [(5, 70001, 160, 32, 1), (3, 2000, 80, 1, 0),
+                                                         (9, 513, 80, 8, 0), (2, 131072, 160, 64, 1)])
+def test_bucketize_long_rows_bitexact(O, dev, n_cols, c_in, T, delta, tb_mode):
+    """Long rows (flattened FC inputs) take the CTA-per-row kernel."""
+    from vdttfs import engine as E
+    rng = np.random.default_rng(c_in + delta)
+    x = spike_map(rng, (n_cols, c_in), fire=0.3, T=T, edges=True)
+    tfs = 40.0 if tb_mode == 0 else 0.0
+    cfg = E.time_cfg_raw(T, delta, tfs)
+    off, cin, tin = E.bucketize(_t(x, dev), n_cols, c_in, cfg, tb_mode=tb_mode)
+    _sync()
+    roff, rcin, rtin, _ = O.bucketize(x, n_cols, c_in, T, delta, tfs, tb_mode)
+    bucket_valid_equal(_np(off), _np(cin), _np(tin), roff, rcin, rtin)
+
+
 @pytest.mark.parametrize("C,H,W,T,delta", [(64, 8, 8, 160, 32), (128, 4, 4, 160, 32),
                                            (2, 16, 16, 160, 16), (128, 5, 3, 100, 8)])
 def test_bucketize_nchw_trunc_bitexact(O, dev, C, H, W, T, delta):

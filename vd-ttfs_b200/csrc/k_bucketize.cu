@@ -14,6 +14,8 @@
 //    and the scatter ranks each lane inside its bin group with
 //    popc(group & lanemask_lt), so equal-bin events keep channel order.
 //    Channel values stay in registers between the two passes (c_in <= 512).
+//  * k_bucketize_rows  -- one CTA per long column (NHWC, c_in > 512), RW warps
+//    over contiguous segments with chunk-major segment offsets.
 //  * k_bucketize_thread -- one thread per column for narrow columns (c_in < 32)
 //    and for NCHW sites, where adjacent threads read adjacent addresses; its
 //    chunk counters live in shared memory laid out [bin][thread] (no bank
@@ -159,8 +161,99 @@ __global__ void __launch_bounds__(128) k_bucketize_thread(BktParams p) {
 
 }  // namespace
 
+// One CTA per long column (NHWC rows with c_in > 512, e.g. a flattened FC
+// input): each of the RW warps owns a contiguous segment of the row.  Pass 1
+// counts the segment's events per chunk (warp-aggregated), the CTA turns the
+// [chunk][warp] counts into exclusive offsets (chunk-major, so segments keep
+// channel order inside a chunk), and pass 2 re-reads each segment and
+// scatters it stably with the same in-window ranking as k_bucketize_warp.
+constexpr int RW = 8;
+
+__global__ void __launch_bounds__(RW * 32) k_bucketize_rows(BktParams p) {
+    extern __shared__ int s_cnt[];                  // [RW][NC] counts, then cursors
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const long long col = blockIdx.x;
+    const int seg = ((p.c_in + RW * 32 - 1) / (RW * 32)) * 32;
+    const int c_lo = warp * seg, c_hi = min(p.c_in, c_lo + seg);
+    int* cnt = s_cnt + warp * p.NC;
+    for (int c = lane; c < p.NC; c += 32) cnt[c] = 0;
+    __syncwarp();
+    const float* src = p.in + col * p.c_in;
+    const unsigned lt = (1u << lane) - 1u;
+    for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
+        const int ch = c0 + lane;
+        const float t = ch < c_hi ? __ldg(src + ch) : p.inf_time;
+        const int b = chunk_bin(t, p);
+        const unsigned grp = __match_any_sync(FULL, b);
+        if (b >= 0 && lane == __ffs(grp) - 1) cnt[b] += __popc(grp);
+        __syncwarp();
+    }
+    __syncthreads();
+    // chunk totals -> exclusive chunk offsets (warp 0), then every warp's
+    // cursor = chunk offset + counts of the earlier segments in that chunk
+    int* off = p.off + col * (long long)(p.NC + 1);
+    if (warp == 0) {
+        int run = 0;
+        for (int c0 = 0; c0 < p.NC; c0 += 32) {
+            const int c = c0 + lane;
+            int v = 0;
+            if (c < p.NC)
+                for (int w = 0; w < RW; ++w) v += s_cnt[w * p.NC + c];
+            int inc = v;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int u = __shfl_up_sync(FULL, inc, d);
+                if (lane >= d) inc += u;
+            }
+            if (c < p.NC) {
+                int base = run + inc - v;
+                off[c] = base;
+                for (int w = 0; w < RW; ++w) {
+                    const int k = s_cnt[w * p.NC + c];
+                    s_cnt[w * p.NC + c] = base;
+                    base += k;
+                }
+            }
+            run += __shfl_sync(FULL, inc, 31);
+        }
+        if (lane == 0) {
+            off[p.NC] = run;
+            if (p.events) atomicAdd(p.events, (unsigned long long)run);
+        }
+    }
+    __syncthreads();
+    int* dc = p.cin + col * p.c_in;
+    float* dt = p.tin + col * p.c_in;
+    for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
+        const int ch = c0 + lane;
+        const float t = ch < c_hi ? __ldg(src + ch) : p.inf_time;
+        const int b = chunk_bin(t, p);
+        const unsigned grp = __match_any_sync(FULL, b);
+        int pos = 0;
+        if (b >= 0) pos = cnt[b] + __popc(grp & lt);
+        __syncwarp();
+        if (b >= 0) {
+            dc[pos] = ch;
+            dt[pos] = t;
+            if (lane == __ffs(grp) - 1) cnt[b] += __popc(grp);
+        }
+        __syncwarp();
+    }
+}
+
 cudaError_t launch_bucketize(const BktParams& p, cudaStream_t s) {
     if (p.n_cols <= 0) return cudaSuccess;
+    if (p.layout == VDT_LAYOUT_NHWC && p.c_in > 512 && p.NC <= 1024) {
+        const size_t smem = (size_t)RW * p.NC * sizeof(int);
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(k_bucketize_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem);
+            if (e != cudaSuccess) return e;
+        }
+        if (p.n_cols >= (1ll << 31)) return cudaErrorInvalidValue;
+        k_bucketize_rows<<<(unsigned)p.n_cols, RW * 32, smem, s>>>(p);
+        return cudaGetLastError();
+    }
     if (p.layout == VDT_LAYOUT_NHWC && p.c_in >= 32 && p.c_in <= 512) {
         const int warps = 8;
         const size_t smem = (size_t)warps * p.NC * sizeof(int);

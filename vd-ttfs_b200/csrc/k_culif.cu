@@ -19,9 +19,12 @@ namespace {
 // One warp per output pixel (n, y, x), lane l owns output channels
 // l*V .. l*V+V-1.  Per chunk the pixel's K*K*C_in input frame windows (delta
 // time bins each, contiguous in memory: frames are [N, C_in, H, W, T]) are
-// staged in shared memory; every lane then forms in[t] for its channels with
-// the reference's FMA order (c_in, ky, kx; out-of-range taps skipped) and
-// scans the chunk.  Frames past T read as 0.
+// staged in shared memory and lane t marks the taps with a nonzero value in
+// bin t.  Each step then walks its marked taps in the reference's order
+// (c_in, ky, kx) with one FMA each: a zero frame value (and an out-of-range
+// tap, which the reference skips) leaves the FMA chain unchanged, since
+// fma(w, 0, acc) = acc for finite w and an accumulator that is never -0.
+// Frames past T read as 0.
 constexpr int C1_WARPS = 4;
 
 template <int V, int DELTA>
@@ -32,8 +35,14 @@ __global__ void __launch_bounds__(C1_WARPS * 32) k_culif_conv1(const float* __re
                                                                int NC, float decay, float th) {
     extern __shared__ float c1_sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int taps = C_in * K * K;
-    float* s_f = c1_sm + warp * taps * DELTA;                 // [taps][DELTA]
+    const int taps = C_in * K * K;                            // <= 32
+    float* s_w = c1_sm;                                       // [taps][C_out]
+    float* s_f = c1_sm + taps * C_out + warp * taps * DELTA;  // [taps][DELTA]
+    for (int i = threadIdx.x; i < taps * C_out; i += blockDim.x) {
+        const int q = i / C_out, co = i - q * C_out;
+        s_w[i] = __ldg(w_oihw + (long long)co * taps + q);
+    }
+    __syncthreads();
     const long long gw = (long long)blockIdx.x * C1_WARPS + warp;
     if (gw >= (long long)N * H * W) return;
     const int x = (int)(gw % W);
@@ -42,14 +51,13 @@ __global__ void __launch_bounds__(C1_WARPS * 32) k_culif_conv1(const float* __re
     const int pad = K / 2;
     const int c0 = lane * V;
     const bool lane_ok = c0 < C_out;
+    const float* wl = s_w + (lane_ok ? c0 : 0);
 
     CulifLanes<V> nu;
     nu.init(lane_ok, 9999.0f);
     const CulifCfg cc{decay, th};
     for (int tau = 0; tau < NC; ++tau) {
         const int base = tau * DELTA;
-        // stage: tap q = (ci*K + ky)*K + kx, bin t -> frame value (0 when the
-        // tap is outside the map or t >= T)
         for (int i = lane; i < taps * DELTA; i += 32) {
             const int q = i / DELTA, t = i - q * DELTA;
             const int ci = q / (K * K), r = q - ci * K * K, ky = r / K, kx = r - ky * K;
@@ -60,31 +68,26 @@ __global__ void __launch_bounds__(C1_WARPS * 32) k_culif_conv1(const float* __re
             s_f[i] = v;
         }
         __syncwarp();
-        float in[DELTA][V];
+        unsigned mask = 0;                                    // lane t: taps with input in bin t
+        if (lane < DELTA)
+            for (int q = 0; q < taps; ++q) mask |= (s_f[q * DELTA + lane] != 0.0f ? 1u : 0u) << q;
+#pragma unroll 4
+        for (int t = 0; t < DELTA; ++t) {
+            unsigned m = __shfl_sync(FULL_MASK, mask, t);
+            float in[V];
 #pragma unroll
-        for (int t = 0; t < DELTA; ++t)
-#pragma unroll
-            for (int v = 0; v < V; ++v) in[t][v] = 0.0f;
-        for (int q = 0; q < taps; ++q) {
-            const int ci = q / (K * K), r = q - ci * K * K, ky = r / K, kx = r - ky * K;
-            const int iy = y + ky - pad, ix = x + kx - pad;
-            if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;   // warp-uniform
-            float wv[V];
-#pragma unroll
-            for (int v = 0; v < V; ++v)
-                wv[v] = lane_ok ? __ldg(w_oihw + (long long)(c0 + v) * taps + q) : 0.0f;
-#pragma unroll
-            for (int t = 0; t < DELTA; ++t) {
+            for (int v = 0; v < V; ++v) in[v] = 0.0f;
+            while (m) {                                       // warp-uniform
+                const int q = __ffs(m) - 1;
+                m &= m - 1;
                 const float f = s_f[q * DELTA + t];
 #pragma unroll
-                for (int v = 0; v < V; ++v) in[t][v] = fmaf(wv[v], f, in[t][v]);
+                for (int v = 0; v < V; ++v) in[v] = fmaf(wl[q * C_out + v], f, in[v]);
             }
+#pragma unroll
+            for (int v = 0; v < V; ++v) nu.step(base + t, in[v], v, cc);
         }
         __syncwarp();
-#pragma unroll
-        for (int t = 0; t < DELTA; ++t)
-#pragma unroll
-            for (int v = 0; v < V; ++v) nu.step(base + t, in[t][v], v, cc);
         if (!__any_sync(FULL_MASK, nu.any())) break;
     }
     if (lane_ok) {
@@ -223,7 +226,7 @@ unsigned grid_1d(long long n, int threads) {
 template <int V, int DELTA>
 cudaError_t launch_conv1_vd(const float* frames, const float* w, float* out, int N, int C_in, int C_out, int H,
                             int W, int K, int T, int NC, float decay, float th, cudaStream_t s) {
-    const size_t smem = (size_t)C1_WARPS * C_in * K * K * DELTA * sizeof(float);
+    const size_t smem = ((size_t)C1_WARPS * DELTA + C_out) * C_in * K * K * sizeof(float);
     auto kern = k_culif_conv1<V, DELTA>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -251,8 +254,8 @@ cudaError_t launch_conv1_v(const float* frames, const float* w, float* out, int 
 
 bool culif_conv1_supported(int C_in, int C_out, int K, int delta) {
     if (delta != 8 && delta != 16 && delta != 32) return false;
-    if (C_out > 128 || K > 7) return false;
-    return (size_t)C1_WARPS * C_in * K * K * delta * sizeof(float) <= 200 * 1024;
+    if (C_out > 128 || C_in * K * K > 32) return false;       // tap mask in one word
+    return ((size_t)C1_WARPS * delta + C_out) * C_in * K * K * sizeof(float) <= 200 * 1024;
 }
 
 cudaError_t launch_culif_conv1(const float* frames, const float* w_oihw, float* out, int N, int C_in, int C_out,

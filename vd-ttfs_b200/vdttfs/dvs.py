@@ -17,6 +17,7 @@ and are permuted once on the device (DvsWeights).
 from __future__ import annotations
 
 import ctypes as C
+import dataclasses
 
 import numpy as np
 
@@ -112,15 +113,28 @@ def fc2(buckets, w_t, N, F_in, F_out, spec, stream=None):
     return out
 
 
+def internal_spec(spec: nets.DvsSpec) -> nets.DvsSpec:
+    """Chunk width the engine runs a network at.  Every stage's result is the
+    same for any chunk width dividing T (each neuron sees the same per-step
+    inputs in the same order; the scan ends at T), so when the configured
+    width divides T the engine buckets at 8 (narrower per-chunk slot tables,
+    four channels per lane); otherwise the configured width is kept, with the
+    reference's scan past T in the last chunk."""
+    if spec.T % spec.delta == 0 and spec.T % 8 == 0:
+        return dataclasses.replace(spec, delta=8)
+    return spec
+
+
 def run(spec: nets.DvsSpec, w: DvsWeights, frames, keep=False, stream=None):
     """The reference main's per-batch sequence (t3:262-296) on the device:
     frames [N, C_in, H, W, T] -> maps, outputs [N, classes], predictions."""
+    spec0, spec = spec, internal_spec(spec)
     N = frames.shape[0]
     s = spec.stage_shapes()
     c1n, c2n, c3n = spec.convs
     H, W = spec.H, spec.W
     maps = []
-    x = conv1_raw(frames, w.conv1, spec, stream)
+    x = conv1_raw(frames, w.conv1, spec0, stream)             # frame windows of the configured width
     maps.append(x)
     x = conv_bucketed(bucketize_sites(x, N, c1n, H, W, spec, stream), w.conv2, N, c1n, c2n, H, W, spec,
                       stream=stream)
