@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(256) k_bucketize_warp(BktParams p) {
     const float* src = p.in + col * p.c_in;
     const int nb = (p.c_in + 31) >> 5;
     float tv[MAXR];
-    // pass 1: warp-aggregated histogram
+    // pass 1: per-chunk counts (shared-memory atomics)
 #pragma unroll
     for (int j = 0; j < MAXR; ++j) {
         if (j < nb) {
@@ -64,11 +64,10 @@ __global__ void __launch_bounds__(256) k_bucketize_warp(BktParams p) {
             const float t = ch < p.c_in ? __ldg(src + ch) : p.inf_time;
             tv[j] = t;
             const int b = chunk_bin(t, p);
-            const unsigned grp = __match_any_sync(FULL, b);
-            if (b >= 0 && lane == __ffs(grp) - 1) cnt[b] += __popc(grp);
-            __syncwarp();
+            if (b >= 0) atomicAdd(&cnt[b], 1);          // counts only: order is free
         }
     }
+    __syncwarp();
     // exclusive scan of the NC counters -> offsets; cnt becomes the cursor
     int* off = p.off + col * (long long)(p.NC + 1);
     int run = 0;

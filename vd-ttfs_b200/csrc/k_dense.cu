@@ -129,14 +129,12 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
             }
         }
     }
-    // 1. histogram by step
+    // 1. histogram by step (shared-memory atomics)
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-        const int tb = key[r] < 0 ? -1 : (key[r] & 0xffff);
-        const unsigned g = __match_any_sync(FULL_MASK, tb);
-        if (tb >= 0 && lane == __ffs(g) - 1) s_bin[tb] += __popc(g);
-        __syncwarp();
+        if (key[r] >= 0) atomicAdd(&s_bin[key[r] & 0xffff], 1);   // counts only: order is free
     }
+    __syncwarp();
     // 2. exclusive scan over steps, then the stable scatter of records
     //    {element offset of the weight row, LUT value}
     int run = 0;

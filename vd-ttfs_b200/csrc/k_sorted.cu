@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
             const int segn = min(SEG, total - s0);
             for (int i = lane; i < DELTA; i += 32) s_cnt[i] = 0;
             __syncwarp();
-            // 1. decode + per-slot histogram
+            // 1. decode + per-slot histogram (shared-memory atomics)
             for (int w0 = 0; w0 < segn; w0 += 32) {
                 const int q = w0 + lane;
                 int slot = -1;
@@ -237,10 +237,9 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
                     slot = tb - base;
                     s_tmp[q] = make_int2((s_wrow[lo] + ci) | (slot << 24), __float_as_int(lv));
                 }
-                const unsigned g = __match_any_sync(FULL_MASK, slot);
-                if (slot >= 0 && lane == __ffs(g) - 1) s_cnt[slot] += __popc(g);
-                __syncwarp();
+                if (slot >= 0) atomicAdd(&s_cnt[slot], 1);   // counts only: order is free
             }
+            __syncwarp();
             // 2. slot offsets, the stable scatter into slot order
             for (int c = 0; c < DELTA; c += 32) {
                 const int i = c + lane;
