@@ -337,7 +337,7 @@ def layer_events(E, net, layers, x_dev, B, dev):
     per = []
     # run the network layer by layer through the per-stage API
     maps = None
-    ctx = E.Context(E.Model(net, layers), B)
+    ctx = E.Context(E.Model(net, layers, device=dev.index), B)
     maps, _, _ = ctx.trace(x_dev, pixels=True)
     cfg = E.time_cfg(net)
     enc = E.encode_image(x_dev.reshape(-1), net.encoder, net.tc_in, net.td_in, net.T).reshape(x_dev.shape)

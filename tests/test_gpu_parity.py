@@ -358,6 +358,26 @@ def test_infer_host_matches_device_and_eager(O, dev):
     assert bits_equal(o4, o2[:3])
 
 
+def test_host_buffers_are_rejected_before_any_launch(dev):
+    """A host buffer where device memory is required fails with
+    VDT_ERR_INVALID (checked on the host, nothing is launched)."""
+    import torch
+    from vdttfs import engine as E, nets, synth
+    net = nets.lenet5()
+    ctx = E.Context(E.Model(net, synth.kaiming_layers(net, 1)), 4)
+    x_host = torch.zeros((4, net.in_h, net.in_w, net.in_c), dtype=torch.float32).pin_memory()
+    with pytest.raises(E.VdtError) as ei:
+        ctx.infer(x_host)
+    assert ei.value.status == 1
+    y = torch.zeros(4 * 8 * 8 * 6, dtype=torch.float32, device=dev)
+    with pytest.raises(E.VdtError) as ei:
+        E.pooling(x_host.reshape(-1)[: y.numel()], 4, 8, 8, 6)
+    assert ei.value.status == 1
+    out, pred = ctx.infer(torch.zeros((4, net.in_h, net.in_w, net.in_c), device=dev))
+    _sync()
+    assert out.shape == (4, net.n_classes)
+
+
 def test_capacity_and_argument_errors(dev):
     from vdttfs import engine as E
     from vdttfs._lib import VdtError

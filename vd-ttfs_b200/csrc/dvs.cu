@@ -23,7 +23,8 @@ extern "C" int vdt_dvs_conv1_raw(const float* d_frames, const float* d_w_oihw, i
         K % 2 == 0 || !culif_ok(T, delta))
         return api_fail(VDT_ERR_INVALID, "bad conv1_raw arguments");
     if (!culif_conv1_supported(C_in, C_out, K, delta))
-        return api_fail(VDT_ERR_UNSUPPORTED, "conv1_raw needs delta in {8,16,32}, C_out <= 128, K <= 7");
+        return api_fail(VDT_ERR_UNSUPPORTED, "conv1_raw needs delta in {8,16,32}, C_out <= 128, C_in*K*K <= 32");
+    if (int s = api_check_buffers(-1, {d_frames, d_w_oihw, d_out})) return s;
     return cuda_status(launch_culif_conv1(d_frames, d_w_oihw, d_out, N, C_in, C_out, H, W, K, T, delta, decay, th,
                                           static_cast<cudaStream_t>(stream)),
                        "conv1_raw launch");
@@ -40,6 +41,7 @@ extern "C" int vdt_dvs_conv_bucketed(const int* d_off, const int* d_cin, const f
     if (out_layout != VDT_LAYOUT_NHWC && out_layout != VDT_LAYOUT_NCHW) return api_fail(VDT_ERR_INVALID, "out_layout");
     if (!culif_supported(K, 0, delta, C_in, C_out, T))
         return api_fail(VDT_ERR_UNSUPPORTED, "delta must be a power of two <= 64 and K*K <= 32");
+    if (int s = api_check_buffers(-1, {d_off, d_cin, d_tin, d_w_hwio, d_out})) return s;
     IntegParams ip{};
     ip.off = d_off; ip.cin = d_cin; ip.tin = d_tin; ip.W = d_w_hwio; ip.out = d_out;
     ip.B = N; ip.H_in = H; ip.W_in = W; ip.C_in = C_in; ip.H_out = H; ip.W_out = W; ip.C_out = C_out;
@@ -58,6 +60,7 @@ extern "C" int vdt_dvs_fc2(const int* d_off, const int* d_cin, const float* d_ti
         return api_fail(VDT_ERR_INVALID, "bad fc2_bucketed_early arguments");
     if (!culif_supported(1, 1, delta, F_in, F_out, T))
         return api_fail(VDT_ERR_UNSUPPORTED, "delta must be a power of two <= 64");
+    if (int s = api_check_buffers(-1, {d_off, d_cin, d_tin, d_w_t, d_out})) return s;
     IntegParams ip{};
     ip.off = d_off; ip.cin = d_cin; ip.tin = d_tin; ip.W = d_w_t; ip.out = d_out;
     ip.B = N; ip.H_in = 1; ip.W_in = 1; ip.C_in = F_in; ip.H_out = 1; ip.W_out = 1; ip.C_out = F_out;
@@ -73,6 +76,7 @@ extern "C" int vdt_dvs_pool(const float* d_in, float* d_out, int N, int C, int H
     if (!d_in || !d_out || N < 0 || C <= 0 || H_in < 2 || W_in < 2 || !culif_ok(T, delta) ||
         (layout != VDT_LAYOUT_NHWC && layout != VDT_LAYOUT_NCHW))
         return api_fail(VDT_ERR_INVALID, "bad pool_chunk_early arguments");
+    if (int s = api_check_buffers(-1, {d_in, d_out})) return s;
     return cuda_status(launch_culif_pool(d_in, d_out, N, C, H_in, W_in, layout, T, delta, decay, th,
                                          static_cast<cudaStream_t>(stream)),
                        "pool_chunk_early launch");
@@ -87,6 +91,7 @@ extern "C" int vdt_dvs_fc1_recurrent(const int* d_off, const int* d_cin, const f
         return api_fail(VDT_ERR_INVALID, "bad fc1_bucketed_recurrent arguments");
     if (F_out % 32 != 0 || F_out > 1024)
         return api_fail(VDT_ERR_UNSUPPORTED, "F_out must be a multiple of 32, at most 1024");
+    if (int s = api_check_buffers(-1, {d_off, d_cin, d_tin, d_w_t, d_wrec_t, d_out})) return s;
     return cuda_status(launch_culif_fc1_rec(d_off, d_cin, d_tin, d_w_t, d_wrec_t, d_out, N, F_in, F_out, T, delta,
                                             decay, th, static_cast<cudaStream_t>(stream)),
                        "fc1_bucketed_recurrent launch");
@@ -95,6 +100,7 @@ extern "C" int vdt_dvs_fc1_recurrent(const int* d_off, const int* d_cin, const f
 extern "C" int vdt_oihw_to_hwio(const float* d_src, float* d_dst, int O, int I, int K, vdt_stream stream) {
     api_clear_error();
     if (!d_src || !d_dst || O <= 0 || I <= 0 || K <= 0) return api_fail(VDT_ERR_INVALID, "bad permute arguments");
+    if (int s = api_check_buffers(-1, {d_src, d_dst})) return s;
     return cuda_status(launch_oihw_to_hwio(d_src, d_dst, O, I, K, static_cast<cudaStream_t>(stream)),
                        "weight permute launch");
 }

@@ -80,6 +80,7 @@ extern "C" int vdt_conv_layer_noalloc(const float* d_in, int tb_mode, const floa
     if (off_bytes + 2 * list_bytes > kScratchBytes)
         return api_fail(VDT_ERR_CAPACITY, "layer needs more bucket scratch than VDT_NOALLOC_SCRATCH_BYTES");
     if (B == 0) return VDT_OK;
+    if (int s = api_check_buffers(-1, {d_in, d_kernel, d_bias, d_decay, d_th, d_out})) return s;
 
     void* base = nullptr;
     cudaError_t e = scratch_address(&base);

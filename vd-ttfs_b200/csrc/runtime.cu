@@ -15,6 +15,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <map>
 #include <mutex>
 #include <string>
@@ -85,10 +86,36 @@ int check_cfg(const vdt_time_cfg* c) {
     return VDT_OK;
 }
 
+// Device buffers handed to a call must live on the device the call runs on
+// (or be managed memory): a buffer of another GPU would otherwise be read by
+// the kernels as a bad address.  dev < 0 means the current device.
+int check_device_buffers(int dev, std::initializer_list<const void*> ptrs) {
+    if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(VDT_ERR_CUDA, "no current device");
+    }
+    for (const void* p : ptrs) {
+        if (!p) continue;
+        cudaPointerAttributes a{};
+        if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(VDT_ERR_INVALID, "buffer %p is not a CUDA allocation", p);
+        }
+        if (a.type == cudaMemoryTypeManaged) continue;
+        if (a.type != cudaMemoryTypeDevice)
+            return fail(VDT_ERR_INVALID, "buffer %p is host memory, a device buffer is required", p);
+        if (a.device != dev)
+            return fail(VDT_ERR_INVALID, "buffer %p lives on device %d, the call runs on device %d", p,
+                        a.device, dev);
+    }
+    return VDT_OK;
+}
+
 }  // namespace
 
 namespace vdt {
 void api_clear_error() { g_last_error.clear(); }
+int api_check_buffers(int dev, std::initializer_list<const void*> ptrs) { return check_device_buffers(dev, ptrs); }
 int api_fail(int status, const char* msg) { return fail(status, "%s", msg); }
 int api_cuda_fail(cudaError_t e, const char* what) { return cuda_fail(e, what); }
 int api_check_cfg(const vdt_time_cfg* c) { return check_cfg(c); }
@@ -715,6 +742,7 @@ extern "C" int vdt_infer(vdt_ctx* c, const float* d_input, int input_is_pixels, 
     g_last_error.clear();
     if (int s = check_batch(c, batch)) return s;
     if (!d_input || !d_out) return fail(VDT_ERR_INVALID, "d_input/d_out is NULL");
+    if (int s = check_device_buffers(c->m->device, {d_input, d_out, d_pred})) return s;
     DeviceGuard g(c->m->device);
     const vdt_model* m = c->m;
     const size_t in_n = (size_t)batch * m->net.in_h * m->net.in_w * m->net.in_c;
@@ -758,6 +786,9 @@ extern "C" int vdt_infer_trace(vdt_ctx* c, const float* d_input, int input_is_pi
     g_last_error.clear();
     if (int s = check_batch(c, batch)) return s;
     if (!d_input || !d_out || !d_layer_out) return fail(VDT_ERR_INVALID, "NULL buffer");
+    if (int s = check_device_buffers(c->m->device, {d_input, d_out, d_pred})) return s;
+    for (size_t i = 0; i < c->m->layers.size(); ++i)
+        if (int s = check_device_buffers(c->m->device, {d_layer_out[i]})) return s;
     DeviceGuard g(c->m->device);
     return enqueue(c, d_input, input_is_pixels, batch, d_out, d_pred, d_layer_out);
 }
@@ -768,6 +799,7 @@ extern "C" int vdt_build_luts(int T, int decay_len, float tc_integ, float td_int
                               vdt_stream stream) {
     g_last_error.clear();
     if (T < 1 || decay_len < 1 || !d_decay || !d_th) return fail(VDT_ERR_INVALID, "bad LUT arguments");
+    if (int s = check_device_buffers(-1, {d_decay, d_th})) return s;
     const LutJob j{tc_integ, td_integ, tc_fire, td_fire, d_decay, d_th};
     VDT_CUDA(launch_build_lut_one(j, T, decay_len, vth_init, static_cast<cudaStream_t>(stream)));
     return VDT_OK;
@@ -777,6 +809,7 @@ extern "C" int vdt_encode(const float* d_pixels, float* d_spikes, int64_t n, int
                           float td, int T, float inf_time, vdt_stream stream) {
     g_last_error.clear();
     if (!d_pixels || !d_spikes || n < 0) return fail(VDT_ERR_INVALID, "bad encode arguments");
+    if (int s = check_device_buffers(-1, {d_pixels, d_spikes})) return s;
     if (encoder != VDT_ENC_LOG && encoder != VDT_ENC_LINEAR) return fail(VDT_ERR_INVALID, "encoder=%d", encoder);
     VDT_CUDA(launch_encode(d_pixels, d_spikes, n, encoder, tc, td, T, inf_time, static_cast<cudaStream_t>(stream)));
     return VDT_OK;
@@ -792,6 +825,7 @@ extern "C" int vdt_bucketize(const float* d_in, int64_t n_cols, int c_in, int la
     if (layout == VDT_LAYOUT_NCHW && (hw <= 0 || n_cols % hw != 0))
         return fail(VDT_ERR_INVALID, "NCHW needs hw > 0 dividing n_cols");
     if (tb_mode != VDT_TB_FLOOR_STAGGER && tb_mode != VDT_TB_TRUNC) return fail(VDT_ERR_INVALID, "tb_mode");
+    if (int s = check_device_buffers(-1, {d_in, d_off, d_cin, d_tin})) return s;
     BktParams p{};
     p.in = d_in; p.n_cols = n_cols; p.c_in = c_in; p.layout = layout; p.hw = hw < 1 ? 1 : hw;
     p.T = cfg->T; p.delta = cfg->delta; p.NC = (cfg->T + cfg->delta - 1) / cfg->delta;
@@ -816,6 +850,7 @@ extern "C" int vdt_conv_bucketed(const int* d_off, const int* d_cin, const float
         return fail(VDT_ERR_INVALID, "bad shape");
     if (!integrate_supported(K, is_fc, cfg->delta, C_out, cfg->T, cfg->decay_len))
         return fail(VDT_ERR_UNSUPPORTED, "delta must be a power of two <= 64 and K*K <= 32");
+    if (int s = check_device_buffers(-1, {d_off, d_cin, d_tin, d_kernel, d_bias, d_decay, d_th, d_out})) return s;
     IntegParams ip{};
     ip.off = d_off; ip.cin = d_cin; ip.tin = d_tin;
     ip.W = d_kernel; ip.bias = d_bias; ip.lut_decay = d_decay; ip.lut_th = d_th; ip.out = d_out;
@@ -836,6 +871,7 @@ extern "C" int vdt_layer_vmem(const float* d_in, const float* d_kernel, const fl
     if (int s = check_cfg(cfg)) return s;
     if (!d_in || !d_kernel || !d_bias || !d_decay || !d_out || B < 0 || C_in <= 0 || C_out <= 0)
         return fail(VDT_ERR_INVALID, "bad vmem arguments");
+    if (int s = check_device_buffers(-1, {d_in, d_kernel, d_bias, d_decay, d_out})) return s;
     cudaError_t e = launch_layer_vmem(d_in, d_kernel, d_bias, d_decay, B, C_in, C_out, cfg->T,
                                       cfg->fire_start, cfg->inf_time, d_out, static_cast<cudaStream_t>(stream));
     if (e == cudaErrorInvalidValue) return fail(VDT_ERR_UNSUPPORTED, "C_in too large for the vmem kernel");
@@ -847,6 +883,7 @@ extern "C" int vdt_pool_min(const float* d_in, float* d_out, int B, int H_in, in
                             float inf_time, vdt_stream stream) {
     g_last_error.clear();
     if (!d_in || !d_out || B < 0 || H_in < 2 || W_in < 2 || C <= 0) return fail(VDT_ERR_INVALID, "bad pool arguments");
+    if (int s = check_device_buffers(-1, {d_in, d_out})) return s;
     VDT_CUDA(launch_pool_min(d_in, d_out, B, H_in, W_in, C, inf_time, static_cast<cudaStream_t>(stream)));
     return VDT_OK;
 }
@@ -856,6 +893,7 @@ extern "C" int vdt_readout(const float* d_out, int B, int K, int mode, float inf
     g_last_error.clear();
     if (!d_out || !d_pred || B < 0 || K <= 0) return fail(VDT_ERR_INVALID, "bad readout arguments");
     if (mode < VDT_READ_ARGMIN_FIRST || mode > VDT_READ_ARGMAX) return fail(VDT_ERR_INVALID, "mode=%d", mode);
+    if (int s = check_device_buffers(-1, {d_out, d_pred})) return s;
     VDT_CUDA(launch_readout(d_out, B, K, mode, inf_time, d_pred, static_cast<cudaStream_t>(stream)));
     return VDT_OK;
 }

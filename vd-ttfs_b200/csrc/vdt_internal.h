@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <initializer_list>
 
 #include "vdttfs.h"
 
@@ -14,6 +15,8 @@ void api_clear_error();
 int api_fail(int status, const char* msg);
 int api_cuda_fail(cudaError_t e, const char* what);
 int api_check_cfg(const vdt_time_cfg* c);
+// every non-null pointer is device memory of `dev` (< 0: the current device)
+int api_check_buffers(int dev, std::initializer_list<const void*> ptrs);
 
 // ---------------------------------------------------------------- bucketize
 struct BktParams {
