@@ -67,6 +67,9 @@ def lib():
         L.orc_dvs_fc1_rec.argtypes = [_ip, _ip, _fp, _fp, _fp] + [C.c_int] * 5 + [C.c_float, C.c_float, _fp]
         L.orc_dvs_fc2.argtypes = [_ip, _ip, _fp, _fp] + [C.c_int] * 5 + [C.c_float, C.c_float, _fp]
         L.orc_dvs_fc2.restype = C.c_longlong
+        L.orc_set_threads.argtypes = [C.c_int]
+        L.orc_set_threads.restype = C.c_int
+        L.orc_set_threads(os.cpu_count() or 1)
         _lib = L
     return _lib
 

@@ -481,3 +481,18 @@ long long orc_dvs_fc2(const int* off, const int* bcin, const float* btin, const 
 }
 
 int orc_max_delta(void) { return ORC_MAX_DELTA; }
+
+/* OpenMP worker count for every later call (launchers such as torchrun set
+   OMP_NUM_THREADS=1 per process; the CPU baselines use all host cores). */
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+int orc_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
+}
