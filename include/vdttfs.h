@@ -95,6 +95,13 @@ typedef struct {
 } vdt_net_desc;
 
 const char* vdt_version(void);
+/* Launch overlap (no counterpart in the reference): 1 lets each kernel of a
+   batch start while its predecessor's last CTAs finish (CUDA programmatic
+   dependent launch; every kernel still waits for its inputs), 0 (default)
+   launches them one after the other.  Process-wide; returns the previous
+   setting.  Results do not change.  Graphs already captured keep the
+   setting they were captured with. */
+int vdt_set_launch_overlap(int enable);
 const char* vdt_strerror(int status);
 const char* vdt_last_error(void);
 

@@ -358,6 +358,35 @@ def test_infer_host_matches_device_and_eager(O, dev):
     assert bits_equal(o4, o2[:3])
 
 
+def test_launch_overlap_changes_nothing(O, dev):
+    """Programmatic dependent launch on and off: identical maps and outputs,
+    through the captured graph and the eager path."""
+    from vdttfs import engine as E
+    from vdttfs._lib import lib
+    net, layers, img = _net_case("vgg16", 7, 3, 0.0)
+    m = E.Model(net, layers, lut_source=E.LUT_HOST_LIBM)
+    ctx = E.Context(m, 7)
+    x = _t(img, dev)
+    prev = lib().vdt_set_launch_overlap(0)
+    try:
+        o0, p0 = ctx.infer(x, pixels=True)
+        maps0, _, _ = ctx.trace(x, pixels=True)
+        o0, p0, maps0 = _np(o0), _np(p0), [_np(mm) for mm in maps0]
+        lib().vdt_set_launch_overlap(1)
+        ctx2 = E.Context(m, 7)                         # fresh graphs, captured with overlap
+        for _ in range(3):
+            o1, p1 = ctx2.infer(x, pixels=True)
+        maps1, _, _ = ctx2.trace(x, pixels=True)
+        _sync()
+        assert bits_equal(_np(o1), o0) and np.array_equal(_np(p1), p0)
+        for a, b in zip(maps0, maps1):
+            assert bits_equal(a, _np(b))
+        spikes = O.encode_linear(img, net.T)
+        assert bits_equal(o0, O.run_net(net, layers, spikes)["out"])
+    finally:
+        lib().vdt_set_launch_overlap(prev)
+
+
 def test_host_buffers_are_rejected_before_any_launch(dev):
     """A host buffer where device memory is required fails with
     VDT_ERR_INVALID (checked on the host, nothing is launched)."""

@@ -46,6 +46,8 @@ __device__ __forceinline__ int chunk_bin(float t, const BktParams& p) {
 template <int MAXR>
 __global__ void __launch_bounds__(256) k_bucketize_warp(BktParams p) {
     extern __shared__ int s_bins[];                 // [warps][NC]
+    chain_release();
+    chain_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long long col = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
     if (col >= p.n_cols) return;                    // warp-uniform
@@ -113,6 +115,8 @@ __global__ void __launch_bounds__(256) k_bucketize_warp(BktParams p) {
 }
 
 __global__ void __launch_bounds__(128) k_bucketize_thread(BktParams p) {
+    chain_release();
+    chain_wait();
     extern __shared__ int s_cnt[];                  // [NC][blockDim]
     const long long col = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const bool live = col < p.n_cols;
@@ -170,6 +174,8 @@ constexpr int RW = 8;
 
 __global__ void __launch_bounds__(RW * 32) k_bucketize_rows(BktParams p) {
     extern __shared__ int s_cnt[];                  // [RW][NC] counts, then cursors
+    chain_release();
+    chain_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long long col = blockIdx.x;
     const int seg = ((p.c_in + RW * 32 - 1) / (RW * 32)) * 32;
@@ -250,18 +256,15 @@ cudaError_t launch_bucketize(const BktParams& p, cudaStream_t s) {
             if (e != cudaSuccess) return e;
         }
         if (p.n_cols >= (1ll << 31)) return cudaErrorInvalidValue;
-        k_bucketize_rows<<<(unsigned)p.n_cols, RW * 32, smem, s>>>(p);
-        return cudaGetLastError();
+        return launch_chain(k_bucketize_rows, dim3((unsigned)p.n_cols), dim3(RW * 32), smem, s, p);
     }
     if (p.layout == VDT_LAYOUT_NHWC && p.c_in >= 32 && p.c_in <= 512) {
         const int warps = 8;
         const size_t smem = (size_t)warps * p.NC * sizeof(int);
         const long long blocks = (p.n_cols + warps - 1) / warps;
         if (p.c_in <= 128)
-            k_bucketize_warp<4><<<(unsigned)blocks, warps * 32, smem, s>>>(p);
-        else
-            k_bucketize_warp<16><<<(unsigned)blocks, warps * 32, smem, s>>>(p);
-        return cudaGetLastError();
+            return launch_chain(k_bucketize_warp<4>, dim3((unsigned)blocks), dim3(warps * 32), smem, s, p);
+        return launch_chain(k_bucketize_warp<16>, dim3((unsigned)blocks), dim3(warps * 32), smem, s, p);
     }
     const int threads = 128;
     const size_t smem = (size_t)threads * p.NC * sizeof(int);
@@ -272,8 +275,7 @@ cudaError_t launch_bucketize(const BktParams& p, cudaStream_t s) {
         if (e != cudaSuccess) return e;
     }
     const long long blocks = (p.n_cols + threads - 1) / threads;
-    k_bucketize_thread<<<(unsigned)blocks, threads, smem, s>>>(p);
-    return cudaGetLastError();
+    return launch_chain(k_bucketize_thread, dim3((unsigned)blocks), dim3(threads), smem, s, p);
 }
 
 }  // namespace vdt

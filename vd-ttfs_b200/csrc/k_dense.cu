@@ -49,6 +49,7 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
                                                          int n_warps, int groups) {
     extern __shared__ __align__(16) int sm[];
     __shared__ int s_floor, s_mono;
+    chain_release();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
     const int fan = ntaps * p.C_in;
@@ -63,6 +64,7 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
     float* s_thx = s_th + p.T;
     for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
     const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
+    chain_wait();                                            // the input map is complete
 
     const int gw = blockIdx.x * DW + warp;
     if (gw >= n_warps) return;                               // warp-uniform
@@ -228,8 +230,7 @@ cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t 
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    kern<<<(n_warps + DW - 1) / DW, DW * 32, smem, s>>>(p, in, n_warps, groups);
-    return cudaGetLastError();
+    return launch_chain(kern, dim3((n_warps + DW - 1) / DW), dim3(DW * 32), smem, s, p, in, n_warps, groups);
 }
 
 template <int V>

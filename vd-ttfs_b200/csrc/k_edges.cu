@@ -41,6 +41,8 @@ __global__ void k_build_lut_one(LutJob j, int T, int decay_len, float vth) {
 
 __global__ void k_encode(const float* __restrict__ px, float* __restrict__ out, long long n,
                          int encoder, float tc, float td, int T, float inf_time) {
+    chain_release();
+    chain_wait();
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
         const float x = __ldg(px + i);
@@ -68,6 +70,8 @@ __global__ void k_encode(const float* __restrict__ px, float* __restrict__ out, 
 
 __global__ void k_pool_min(const float* __restrict__ in, float* __restrict__ out, int B,
                            int H_in, int W_in, int C, float inf_time) {
+    chain_release();
+    chain_wait();
     const int H_out = H_in / 2, W_out = W_in / 2, C4 = C / 4;
     const long long n = (long long)B * H_out * W_out * C4;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -96,6 +100,8 @@ __global__ void k_pool_min(const float* __restrict__ in, float* __restrict__ out
 
 __global__ void k_pool_min_scalar(const float* __restrict__ in, float* __restrict__ out, int B,
                                   int H_in, int W_in, int C, float inf_time) {
+    chain_release();
+    chain_wait();
     const int H_out = H_in / 2, W_out = W_in / 2;
     const long long n = (long long)B * H_out * W_out * C;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -121,6 +127,8 @@ __global__ void k_layer_vmem(const float* __restrict__ in, const float* __restri
                              int B, int C_in, int C_out, int T, float tfs, float inf_time,
                              float* __restrict__ out) {
     extern __shared__ float s_in[];                  // [warps][C_in] values, then flags
+    chain_release();
+    chain_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long long img = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
     if (img >= B) return;
@@ -149,6 +157,8 @@ __global__ void k_layer_vmem(const float* __restrict__ in, const float* __restri
 
 __global__ void k_readout(const float* __restrict__ out, int B, int K, int mode, float inf_time,
                           int32_t* __restrict__ pred) {
+    chain_release();
+    chain_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     const float* o = out + (long long)b * K;
@@ -192,8 +202,8 @@ cudaError_t launch_build_lut_one(const LutJob& j, int T, int decay_len, float vt
 cudaError_t launch_encode(const float* px, float* out, long long n, int encoder, float tc, float td,
                           int T, float inf_time, cudaStream_t s) {
     if (n <= 0) return cudaSuccess;
-    k_encode<<<grid_for(n, 256), 256, 0, s>>>(px, out, n, encoder, tc, td, T, inf_time);
-    return cudaGetLastError();
+    return launch_chain(k_encode, dim3(grid_for(n, 256)), dim3(256), 0, s, px, out, n, encoder, tc, td, T,
+                        inf_time);
 }
 
 cudaError_t launch_pool_min(const float* in, float* out, int B, int H_in, int W_in, int C,
@@ -202,10 +212,10 @@ cudaError_t launch_pool_min(const float* in, float* out, int B, int H_in, int W_
     if (n <= 0) return cudaSuccess;
     const bool vec = (C % 4 == 0) && ((uintptr_t)in % 16 == 0) && ((uintptr_t)out % 16 == 0);
     if (vec)
-        k_pool_min<<<grid_for(n / 4, 256), 256, 0, s>>>(in, out, B, H_in, W_in, C, inf_time);
-    else
-        k_pool_min_scalar<<<grid_for(n, 256), 256, 0, s>>>(in, out, B, H_in, W_in, C, inf_time);
-    return cudaGetLastError();
+        return launch_chain(k_pool_min, dim3(grid_for(n / 4, 256)), dim3(256), 0, s, in, out, B, H_in, W_in, C,
+                            inf_time);
+    return launch_chain(k_pool_min_scalar, dim3(grid_for(n, 256)), dim3(256), 0, s, in, out, B, H_in, W_in, C,
+                        inf_time);
 }
 
 cudaError_t launch_layer_vmem(const float* in, const float* W, const float* bias,
@@ -215,16 +225,14 @@ cudaError_t launch_layer_vmem(const float* in, const float* W, const float* bias
     const int warps = 4;
     const size_t smem = (size_t)warps * C_in * (sizeof(float) + 1);
     if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    k_layer_vmem<<<(B + warps - 1) / warps, warps * 32, smem, s>>>(in, W, bias, lut_decay, B, C_in,
-                                                                    C_out, T, tfs, inf_time, out);
-    return cudaGetLastError();
+    return launch_chain(k_layer_vmem, dim3((B + warps - 1) / warps), dim3(warps * 32), smem, s, in, W, bias,
+                        lut_decay, B, C_in, C_out, T, tfs, inf_time, out);
 }
 
 cudaError_t launch_readout(const float* out, int B, int K, int mode, float inf_time, int32_t* pred,
                            cudaStream_t s) {
     if (B <= 0) return cudaSuccess;
-    k_readout<<<(B + 127) / 128, 128, 0, s>>>(out, B, K, mode, inf_time, pred);
-    return cudaGetLastError();
+    return launch_chain(k_readout, dim3((B + 127) / 128), dim3(128), 0, s, out, B, K, mode, inf_time, pred);
 }
 
 }  // namespace vdt

@@ -152,6 +152,7 @@ __device__ __forceinline__ int tab_words(int ntaps, int OS) {
 template <int DELTA, int V, int EB, int MINB>
 __global__ void __launch_bounds__(WARPS * 32, MINB) k_integrate(IntegParams p, long long n_warps, int groups) {
     extern __shared__ __align__(16) int smem[];
+    chain_release();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
     const int OS = p.NC + 1;
@@ -177,6 +178,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) k_integrate(IntegParams p, l
         s_min[c] = mn;
     }
     __syncthreads();
+    chain_wait();                                     // the bucket lists are complete
 
     const long long gw = (long long)blockIdx.x * WARPS + warp;
     if (gw >= n_warps) return;                        // warp-uniform
@@ -396,8 +398,7 @@ cudaError_t launch_dv(const IntegParams& p, cudaStream_t s, long long n_warps, i
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    kern<<<(unsigned)blocks, WARPS * 32, smem, s>>>(p, n_warps, groups);
-    return cudaGetLastError();
+    return launch_chain(kern, dim3((unsigned)blocks), dim3(WARPS * 32), smem, s, p, n_warps, groups);
 }
 
 template <int DELTA>

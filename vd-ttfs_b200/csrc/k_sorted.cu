@@ -87,6 +87,7 @@ template <int DELTA, int V, int MINB, bool CULIF>
 __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int n_warps, int groups) {
     extern __shared__ __align__(16) int sm[];
     __shared__ int s_floor, s_mono;
+    chain_release();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
     const int OS = p.NC + 1;
@@ -111,6 +112,7 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
         tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
     }
     const CulifCfg cc{p.culif_decay, p.culif_th};
+    chain_wait();                                            // the bucket lists are complete
 
     const int gw = blockIdx.x * SWARPS + warp;
     if (gw >= n_warps) return;                               // warp-uniform
@@ -346,8 +348,8 @@ cudaError_t launch_sorted_dv(const IntegParams& p, cudaStream_t s, int n_warps, 
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    kern<<<(n_warps + SWARPS - 1) / SWARPS, SWARPS * 32, smem, s>>>(p, n_warps, groups);
-    return cudaGetLastError();
+    return launch_chain(kern, dim3((n_warps + SWARPS - 1) / SWARPS), dim3(SWARPS * 32), smem, s, p, n_warps,
+                        groups);
 }
 
 template <int DELTA, bool CULIF>

@@ -11,6 +11,7 @@
 //    (t2:260,273,280,286); here a batch is one graph launch.
 //  * the per-stage entry points wrap single kernels for drop-in use.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -111,9 +112,16 @@ int check_device_buffers(int dev, std::initializer_list<const void*> ptrs) {
     return VDT_OK;
 }
 
+// launch overlap (programmatic dependent launch): off by default -- on the
+// VGG-16 B=256 step it measured 9.83 ms against 9.62 ms without it
+std::atomic<int> g_overlap{0};
+
 }  // namespace
 
+extern "C" int vdt_set_launch_overlap(int enable) { return g_overlap.exchange(enable != 0 ? 1 : 0); }
+
 namespace vdt {
+bool overlap_enabled() { return g_overlap.load(std::memory_order_relaxed) != 0; }
 void api_clear_error() { g_last_error.clear(); }
 int api_check_buffers(int dev, std::initializer_list<const void*> ptrs) { return check_device_buffers(dev, ptrs); }
 int api_fail(int status, const char* msg) { return fail(status, "%s", msg); }

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <initializer_list>
+#include <utility>
 
 #include "vdttfs.h"
 
@@ -17,6 +18,36 @@ int api_cuda_fail(cudaError_t e, const char* what);
 int api_check_cfg(const vdt_time_cfg* c);
 // every non-null pointer is device memory of `dev` (< 0: the current device)
 int api_check_buffers(int dev, std::initializer_list<const void*> ptrs);
+
+// ------------------------------------------------------- launch overlap (PDL)
+// Kernels of the layer chain are launched with programmatic stream
+// serialization: a kernel's CTAs may start while its predecessor's last wave
+// drains.  Every chained kernel signals chain_release() first and calls
+// chain_wait() before it reads anything a predecessor wrote or writes any
+// global memory; before that it may only read model constants (weights,
+// LUTs) and use shared memory.  griddepcontrol.wait returns once the
+// predecessor grid has completed and its writes are visible (immediately
+// when the kernel was launched without the attribute).
+bool overlap_enabled();
+
+__device__ __forceinline__ void chain_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void chain_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_chain(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = overlap_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------- bucketize
 struct BktParams {

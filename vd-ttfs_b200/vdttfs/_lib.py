@@ -81,6 +81,7 @@ SIGNATURES = {
     "vdt_dvs_fc1_recurrent": (C.c_int, [_vp] * 5 + [C.c_int] * 5 + [C.c_float, C.c_float, _vp, _vp]),
     "vdt_dvs_fc2": (C.c_int, [_vp] * 4 + [C.c_int] * 5 + [C.c_float, C.c_float, _vp, _vp]),
     "vdt_oihw_to_hwio": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, _vp]),
+    "vdt_set_launch_overlap": (C.c_int, [C.c_int]),
     "vdt_noalloc_scratch_bytes": (C.c_size_t, []),
     "vdt_conv_layer_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, C.c_int, C.c_int,
                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
