@@ -42,7 +42,10 @@ CONFIGS = {
     "lenet5": ("lenet5", 2, 65536, 0.8, "strong"),
     "lenet5_b1024": ("lenet5", 1, 1024, 0.8, "weak"),
     "dvs": ("dvs", 4, 64, 0.0, "weak"),     # task-3 CuLIF network, 2x128x128 event frames
+    "vgg16_sweep": ("vgg16", 5, 256, 0.2, "weak"),   # delta x zero fraction x T'
 }
+
+VGG16_DENSE_MACS = 313_725_952      # dense multiply-accumulates of one 3x32x32 VGG-16 image
 
 
 def parse():
@@ -646,11 +649,84 @@ def run_dvs_reference(a):
             "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ------------------------------------------------- config 5: the sweep --
+def sweep_point(E, nets, synth, dev, delta, zf, T, B, steps, warmup, flush):
+    import torch
+    net = nets.vgg16(T=T, delta=delta)
+    layers = synth.kaiming_layers(net, 3)
+    img = synth.images(5, B, net.in_h, net.in_w, net.in_c, zf)
+    model = E.Model(net, layers, device=dev.index)
+    ctx = E.Context(model, B)
+    x = torch.from_numpy(img).to(dev)
+    ctx.set_counting(True)
+    ctx.infer(x, pixels=True)
+    torch.cuda.synchronize()
+    events, fetched = ctx.counters()
+    ctx.set_counting(False)
+    for _ in range(warmup):
+        ctx.infer(x, pixels=True)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ctx.infer(x, pixels=True)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ctx.set_profiling(True)
+    ctx.layer_times()
+    for _ in range(3):
+        flush.fill_(1)
+        ctx.infer(x, pixels=True)
+    bkt, integ, pool, nb = ctx.layer_times()
+    ctx.set_profiling(False)
+    alg = sum(layer_bytes(net, layer_events(E, net, layers, x, B, dev), B))
+    kern_ms = (float(np.sum(bkt)) + float(np.sum(integ))) / nb
+    ms = float(np.mean(times))
+    ctx.close()
+    model.close()
+    return {"delta": delta, "zero_frac": zf, "T": T, "images_per_sec": round(B / (ms / 1e3), 1),
+            "ms_per_step": round(ms, 4), "integrator_gbs": round(alg / (kern_ms / 1e3) / 1e9, 1),
+            "events_per_image": round(events / B, 1),
+            "fetched_synapse_fraction": round(fetched / B / VGG16_DENSE_MACS, 4)}
+
+
+def run_sweep(a):
+    """VGG-16, batch 256, delta in {4,8,16,32,64} x input
+    zero fraction in {0.2,0.5,0.9} x window T' in {80,40,20}.  delta sets the
+    reference's bucket width and with it the fetched-synapse accounting; the
+    engine's integrators are delta-invariant (k_sorted buckets at its own
+    width), so images/s depends on the input and T' only."""
+    import torch
+    from vdttfs import engine as E, nets, synth
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    B = a.batch or 256
+    pts = []
+    for T in (80, 40, 20):
+        for zf in (0.2, 0.5, 0.9):
+            for delta in (4, 8, 16, 32, 64):
+                pts.append(sweep_point(E, nets, synth, dev, delta, zf, T, B, a.steps, a.warmup, flush))
+    head = next(p for p in pts if p["delta"] == 8 and p["zero_frac"] == 0.2 and p["T"] == 80)
+    peak, peak_kind = peaks()
+    return {"metric": "images_per_sec", "value": head["images_per_sec"], "unit": "images/s", "n_gpus": 1,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": "vgg16 C5 sweep (value at delta 8, zero fraction 0.2, T 80)",
+                       "batch_per_gpu": B, "l2": "flushed (256 MiB write) between steps"},
+            "hbm_peak_gbs": peak, "peak_source": peak_kind, "sweep": pts}
+
+
 def main():
     a = parse()
     if a.warmup < 3:
         a.warmup = 3
-    if a.config == "dvs":
+    if a.config == "vgg16_sweep":
+        res = run_sweep(a)
+    elif a.config == "dvs":
         res = run_dvs_reference(a) if a.impl == "reference" else run_dvs_engine(a)
     else:
         res = run_reference(a) if a.impl == "reference" else run_engine(a)
