@@ -309,8 +309,12 @@ def test_every_integrator_choice_is_bitexact(O, dev, kernel):
     assert bits_equal(_np(out), ref["out"]) and np.array_equal(_np(pred), ref["pred"])
     assert events == sum(ref["events"]) and fetched == sum(ref["fetched"])
     ctx.set_counting(False)
-    out2, pred2 = ctx.infer(_t(spikes, dev))
+    maps, out2, pred2 = ctx.trace(_t(spikes, dev))
     _sync()
+    ri = 0
+    for li, l in enumerate(net.layers):
+        assert bits_equal(_np(maps[li]).reshape(-1), ref["maps"][ri]), f"layer {li} differs (no counting)"
+        ri += 2 if l.pool_after else 1
     assert bits_equal(_np(out2), ref["out"])
     with pytest.raises(E.VdtError):
         ctx.set_layer_kernel(len(net.layers) - 1, 0)  # membrane-readout layer
