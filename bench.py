@@ -42,6 +42,7 @@ CONFIGS = {
     "lenet5": ("lenet5", 2, 65536, 0.8, "strong"),
     "lenet5_b1024": ("lenet5", 1, 1024, 0.8, "weak"),
     "dvs": ("dvs", 4, 64, 0.0, "weak"),     # task-3 CuLIF network, 2x128x128 event frames
+    "dvs_ref": ("dvs_ref", 4, 64, 0.0, "weak"),   # the reference's own 2x32x32 DVS network
     "vgg16_sweep": ("vgg16", 5, 256, 0.2, "weak"),   # delta x zero fraction x T'
 }
 
@@ -499,9 +500,9 @@ def run_dvs_engine(a):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    _, cfg_id, Bcfg, _, scaling = CONFIGS["dvs"]
+    netname, cfg_id, Bcfg, _, scaling = CONFIGS[a.config]
     B = a.batch or Bcfg
-    spec = nets.dvs()
+    spec = nets.dvs() if netname == "dvs" else nets.dvs_ref()
     wts = synth.dvs_weights(spec, cfg_id)
     w = dvs.DvsWeights(spec, wts, dev)
     frames = synth.dvs_frames(cfg_id, B, spec, stream=rank)
@@ -582,7 +583,8 @@ def run_dvs_engine(a):
             "ms_per_step": round(tot_ms / a.steps, 4), "higher_is_better": True,
             "scaling": scaling, "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic (seeded Bernoulli(0.05) event frames, Kaiming weights, see vdttfs/synth.py)",
-            "config": {"workload": f"dvs C{cfg_id}", "model": "dvs-culif 2x128x128, 11 classes",
+            "config": {"workload": f"{netname} C{cfg_id}",
+                       "model": f"dvs-culif {spec.in_c}x{spec.H}x{spec.W}, {spec.classes} classes",
                        "global_batch": world * B, "batch_per_gpu": B, "T": spec.T, "delta": spec.delta,
                        "parallelism": f"dp{world}", "l2": "inputs larger than L2 (frames 21 MB per sample)"},
             "e2e": {"value": round(e2e, 1), "unit": "samples/s", "h2d_bytes_per_step": int(frames.nbytes),
@@ -626,8 +628,8 @@ def run_dvs_reference(a):
         return None
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    _, cfg_id, _, _, scaling = CONFIGS["dvs"]
-    spec = nets.dvs()
+    netname, cfg_id, _, _, scaling = CONFIGS[a.config]
+    spec = nets.dvs() if netname == "dvs" else nets.dvs_ref()
     wts = synth.dvs_weights(spec, cfg_id)
     n = 1
     frames = synth.dvs_frames(cfg_id, n, spec, stream=0)
@@ -642,7 +644,7 @@ def run_dvs_reference(a):
     return {"impl": "reference", "metric": "images_per_sec", "value": v, "unit": "samples/s",
             "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt / a.steps * 1e3, 3),
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": f"dvs C{cfg_id}", "batch_per_step": n, "T": spec.T, "delta": spec.delta},
+            "config": {"workload": f"{netname} C{cfg_id}", "batch_per_step": n, "T": spec.T, "delta": spec.delta},
             "cpu_baseline": {"value": v, "unit": "samples/s", "cores": cores, "kind": "port",
                              "sample": f"{n} sample per step, the CPU port of the reference's task-3 "
                                        f"path (oracle/vdt_oracle.c), OpenMP {cores} threads"},
@@ -726,7 +728,7 @@ def main():
         a.warmup = 3
     if a.config == "vgg16_sweep":
         res = run_sweep(a)
-    elif a.config == "dvs":
+    elif a.config in ("dvs", "dvs_ref"):
         res = run_dvs_reference(a) if a.impl == "reference" else run_dvs_engine(a)
     else:
         res = run_reference(a) if a.impl == "reference" else run_engine(a)
