@@ -142,13 +142,17 @@ int vdt_ctx_layer_times(vdt_ctx* c, int n_layers, float* bucketize_ms, float* in
                         float* pool_ms, int* batches);
 
 /* Integrator each layer runs (no counterpart in the reference, which has one
-   kernel).  A layer with VDT_KERNEL_DENSE launches no bucketize pass unless
-   counting is on. */
+   kernel).  A layer with VDT_KERNEL_DENSE or VDT_KERNEL_THREAD launches no
+   bucketize pass unless counting is on (counting passes run a
+   VDT_KERNEL_THREAD layer through k_dense, which keeps the reference's
+   fetched-synapse accounting). */
 enum {
     VDT_KERNEL_CHUNK = 0,   /* k_integrate: chunk-bucket integrator (t2:84-170 order) */
     VDT_KERNEL_SORTED = 1,  /* k_sorted: per-chunk slot-sorted buckets, same results */
     VDT_KERNEL_DENSE = 2,   /* k_dense: bucketing fused, reads the spike map */
-    VDT_KERNEL_VMEM = 3     /* k_layer_vmem membrane readout */
+    VDT_KERNEL_VMEM = 3,    /* k_layer_vmem membrane readout */
+    VDT_KERNEL_THREAD = 4   /* k_thread: one thread per output pixel, bucketing
+                               fused; conv layers with K*K*C_in <= 32, C_out <= 16 */
 };
 int vdt_ctx_layer_kernels(const vdt_ctx* c, int n_layers, int* kernels);
 /* Force the integrator of one layer (-1 = automatic choice); results are the

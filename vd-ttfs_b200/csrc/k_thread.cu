@@ -1,0 +1,141 @@
+// k_thread.cu -- integrator for narrow conv layers (K*K*C_in <= 32 inputs per
+// pixel, C_out <= 16): one thread per output pixel, all of its output
+// channels.  Same results as k_bucketize + k_conv_bucketed (t1:45-162,
+// t2:45-170), bit for bit.
+//
+// A warp of 32 pixels replaces 32 warps of k_dense, which for a 6-channel
+// layer would leave 26 of 32 lanes idle.  The thread reads its pixel's inputs
+// once into registers as keys (step << 18 | input index << 13 | LUT index), so
+// increasing key order is the reference's order: by step, and inside a step
+// by (tap, channel) -- each neuron's FMA chain.  The thread then repeatedly
+// takes the smallest key above the last one (a min over its registers), adds
+// w[input][c] * LUT to every channel's open step, and closes a step when the
+// next key leaves it (lanes.h closes; input-free steps by bisection).
+#include "lanes.h"
+#include "vdt_internal.h"
+
+namespace vdt {
+namespace {
+
+constexpr int TW = 4;             // warps per CTA
+constexpr int TKEYS = 32;         // inputs per pixel held in registers
+constexpr int KEY_NONE = 0x7fffffff;
+
+template <int CO, int MINB>
+__global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const float* __restrict__ in,
+                                                          long long n_pix) {
+    extern __shared__ __align__(16) float tsm[];
+    __shared__ int s_floor, s_mono;
+    chain_release();
+    float* s_decay = tsm;
+    float* s_th = s_decay + p.decay_len;
+    float* s_thx = s_th + p.T;
+    for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
+    const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
+    chain_wait();                                            // the input map is complete
+
+    const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (pix >= n_pix) return;
+    const int w_out = (int)(pix % p.W_out);
+    const long long r = pix / p.W_out;
+    const int h_out = (int)(r % p.H_out);
+    const long long img = r / p.H_out;
+    const int fan = p.K * p.K * p.C_in;
+
+    int key[TKEYS];
+#pragma unroll
+    for (int f = 0; f < TKEYS; ++f) {
+        key[f] = KEY_NONE;
+        if (f < fan) {
+            const int tap = f / p.C_in, c = f - tap * p.C_in;
+            const int kh = tap / p.K, kw = tap - kh * p.K;
+            const int h_in = h_out - p.pad + kh, w_in = w_out - p.pad + kw;
+            if (h_in >= 0 && h_in < p.H_in && w_in >= 0 && w_in < p.W_in) {
+                const float t = __ldg(in + ((img * p.H_in + h_in) * p.W_in + w_in) * p.C_in + c);
+                if (t < p.inf_time) {
+                    int b = (int)floorf(t - p.tfs);
+                    if (b < 0) b = 0;
+                    if (b < p.T) {
+                        int ti;
+                        if (p.lut_mode == VDT_LUT_BY_TB) {
+                            ti = b;
+                        } else {
+                            ti = (int)t;
+                            ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+                        }
+                        key[f] = (b << 18) | (f << 13) | ti;
+                    }
+                }
+            }
+        }
+    }
+
+    Lanes<CO> nu;
+#pragma unroll
+    for (int c = 0; c < CO; ++c) {
+        nu.carry[c] = c < p.C_out ? __ldg(p.bias + c) : 0.0f;
+        nu.res[c] = p.inf_time;
+        nu.acc[c] = 0.0f;
+        nu.alive[c] = c < p.C_out;
+    }
+    int last = -1, cur = -1, next_t = 0;
+    while (nu.any()) {
+        int m = KEY_NONE;
+#pragma unroll
+        for (int f = 0; f < TKEYS; ++f) m = (key[f] > last && key[f] < m) ? key[f] : m;
+        if (m == KEY_NONE) break;
+        const int tb = m >> 18;
+        if (tb != cur) {
+            if (cur >= 0) {
+                nu.close_empty(next_t, cur, tt);
+                nu.close_step_bf(cur, tt);
+                next_t = cur + 1;
+            }
+            cur = tb;
+        }
+        const float lv = s_decay[m & 0x1fff];
+        const float* wr = p.W + ((m >> 13) & 31) * p.C_out;
+#pragma unroll
+        for (int c = 0; c < CO; ++c)
+            if (c < p.C_out) nu.acc[c] = fmaf(__ldg(wr + c), lv, nu.acc[c]);
+        last = m;
+    }
+    if (cur >= 0 && nu.any()) {
+        nu.close_empty(next_t, cur, tt);
+        nu.close_step_bf(cur, tt);
+        next_t = cur + 1;
+    }
+    if (nu.any()) nu.close_empty(next_t, p.T, tt);
+    float* o = p.out + pix * p.C_out;
+#pragma unroll
+    for (int c = 0; c < CO; ++c)
+        if (c < p.C_out) o[c] = nu.res[c];
+}
+
+template <int CO>
+cudaError_t launch_thread_c(const IntegParams& p, const float* in, cudaStream_t s, long long n_pix) {
+    const size_t smem = (size_t)(p.decay_len + 2 * p.T) * sizeof(float);
+    constexpr int REGS = TKEYS + 4 * CO + 40;
+    constexpr int MINB = (65536 / (TW * 32 * REGS)) > 8 ? 8 : (65536 / (TW * 32 * REGS));
+    auto kern = k_thread<CO, MINB>;
+    const long long blocks = (n_pix + TW * 32 - 1) / (TW * 32);
+    if (blocks >= (1ll << 31)) return cudaErrorInvalidValue;
+    return launch_chain(kern, dim3((unsigned)blocks), dim3(TW * 32), smem, s, p, in, n_pix);
+}
+
+}  // namespace
+
+bool thread_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len) {
+    if (is_fc || K * K * C_in > TKEYS || C_out > 16) return false;
+    if (T >= (1 << 13)) return false;                          // 13-bit step / LUT index in the key
+    return (size_t)(decay_len + 2 * T) * sizeof(float) <= 48 * 1024;
+}
+
+cudaError_t launch_thread(const IntegParams& p, const float* in, cudaStream_t s) {
+    const long long n_pix = (long long)p.B * p.H_out * p.W_out;
+    if (n_pix <= 0) return cudaSuccess;
+    if (p.C_out <= 8) return launch_thread_c<8>(p, in, s, n_pix);
+    return launch_thread_c<16>(p, in, s, n_pix);
+}
+
+}  // namespace vdt

@@ -206,7 +206,8 @@ struct vdt_ctx {
 };
 
 namespace {
-// which integrator runs a layer: k_dense (bucketing fused in) for small
+// which integrator runs a layer: k_thread for narrow conv layers (a warp per
+// pixel would leave most lanes idle), k_dense (bucketing fused in) for small
 // per-pixel fan-in, else k_sorted, else the generic chunk integrator
 int layer_kernel(const vdt_ctx* c, int li, const vdt_time_cfg& cfg) {
     const Layer& ly = c->m->layers[li];
@@ -215,6 +216,9 @@ int layer_kernel(const vdt_ctx* c, int li, const vdt_time_cfg& cfg) {
     const int fc = ly.d.kind == VDT_FC;
     const int K = fc ? 1 : ly.d.k;
     const int fan = K * K * ly.C_in;
+    if (thread_supported(ly.d.k, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len) &&
+        dense_supported(ly.d.k, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len))
+        return VDT_KERNEL_THREAD;
     if (fan <= c->dense_max_fan && dense_supported(ly.d.k, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len))
         return VDT_KERNEL_DENSE;
     if (sorted_supported(K, fc, kSortedDelta, ly.C_in, ly.C_out, cfg.T, cfg.decay_len)) return VDT_KERNEL_SORTED;
@@ -531,7 +535,7 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
             ip.lut_mode = cfg.lut_mode; ip.decay_len = cfg.decay_len;
             ip.tfs = cfg.fire_start; ip.inf_time = cfg.inf_time;
             ip.fetched = fe;
-            const bool dense = kern == VDT_KERNEL_DENSE;
+            const bool dense = kern == VDT_KERNEL_DENSE || kern == VDT_KERNEL_THREAD;
             if (!dense || ev) {
                 // the dense path needs no buckets; they are still built when
                 // counting, for the event counter
@@ -553,7 +557,8 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
                 VDT_CUDA(launch_bucketize(bp, s));
             }
             StageTimer st(c, i, 1);
-            if (dense) VDT_CUDA(launch_dense(ip, x, s));
+            if (kern == VDT_KERNEL_THREAD && !fe) VDT_CUDA(launch_thread(ip, x, s));
+            else if (dense) VDT_CUDA(launch_dense(ip, x, s));
             else if (kern == VDT_KERNEL_SORTED) VDT_CUDA(launch_sorted(ip, s));
             else VDT_CUDA(launch_integrate(ip, s));
         }
@@ -692,6 +697,10 @@ extern "C" int vdt_ctx_set_layer_kernel(vdt_ctx* c, int layer, int kernel) {
         case VDT_KERNEL_SORTED: ok = ly.d.out != VDT_OUT_VMEM && sorted_supported(K, fc, kSortedDelta, ly.C_in, ly.C_out, cfg.T, cfg.decay_len); break;
         case VDT_KERNEL_DENSE: ok = ly.d.out != VDT_OUT_VMEM && dense_supported(K, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len); break;
         case VDT_KERNEL_VMEM: ok = ly.d.out == VDT_OUT_VMEM; break;
+        case VDT_KERNEL_THREAD:   // counting passes run the layer through k_dense
+            ok = ly.d.out != VDT_OUT_VMEM && thread_supported(K, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len) &&
+                 dense_supported(K, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len);
+            break;
         default: return fail(VDT_ERR_INVALID, "kernel=%d", kernel);
     }
     if (!ok) return fail(VDT_ERR_UNSUPPORTED, "kernel %d cannot run layer %d", kernel, layer);

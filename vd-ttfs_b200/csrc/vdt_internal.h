@@ -95,6 +95,11 @@ bool integrate_supported(int K, int is_fc, int delta, int C_out, int T, int deca
 cudaError_t launch_dense(const IntegParams& p, const float* in, cudaStream_t s);
 bool dense_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len);
 
+// One thread per output pixel for narrow conv layers (K*K*C_in <= 32,
+// C_out <= 16): reads the NHWC spike map directly, same results.
+cudaError_t launch_thread(const IntegParams& p, const float* in, cudaStream_t s);
+bool thread_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len);
+
 // Chunk integrator with per-chunk slot sorting (reference bucket layout,
 // same results as launch_integrate, fewer instructions per event).
 cudaError_t launch_sorted(const IntegParams& p, cudaStream_t s);

@@ -34,8 +34,8 @@ from .blob import BlobLayer, write_blob
 LUT_DEVICE, LUT_HOST_LIBM = 0, 1
 LAYOUT_NHWC, LAYOUT_NCHW = 0, 1
 TB_FLOOR_STAGGER, TB_TRUNC = 0, 1
-KERNEL_CHUNK, KERNEL_SORTED, KERNEL_DENSE, KERNEL_VMEM = 0, 1, 2, 3
-KERNEL_NAMES = {0: "k_integrate", 1: "k_sorted", 2: "k_dense", 3: "k_layer_vmem"}
+KERNEL_CHUNK, KERNEL_SORTED, KERNEL_DENSE, KERNEL_VMEM, KERNEL_THREAD = 0, 1, 2, 3, 4
+KERNEL_NAMES = {0: "k_integrate", 1: "k_sorted", 2: "k_dense", 3: "k_layer_vmem", 4: "k_thread"}
 
 
 def _ptr(t) -> int:
@@ -144,8 +144,9 @@ class Context:
         return a, b, c, nb.value
 
     def layer_kernels(self):
-        """Integrator per layer: KERNEL_CHUNK, KERNEL_SORTED, KERNEL_DENSE or
-        KERNEL_VMEM (dense layers launch no bucketize pass)."""
+        """Integrator per layer: KERNEL_CHUNK, KERNEL_SORTED, KERNEL_DENSE,
+        KERNEL_THREAD or KERNEL_VMEM (dense and thread layers launch no
+        bucketize pass)."""
         n = len(self.model.net.layers)
         k = np.zeros(n, np.int32)
         check(lib().vdt_ctx_layer_kernels(self.h, n, k.ctypes.data), "vdt_ctx_layer_kernels")
