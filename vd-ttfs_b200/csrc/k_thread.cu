@@ -27,11 +27,24 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     extern __shared__ __align__(16) float tsm[];
     __shared__ int s_floor, s_mono;
     chain_release();
-    float* s_decay = tsm;
+    const int fan = p.K * p.K * p.C_in;
+    // weights padded to CO columns (zeros past C_out), one row per input
+    float* s_w = tsm;                                        // [TKEYS][CO]
+    int4* s_tap = reinterpret_cast<int4*>(s_w + TKEYS * CO); // per input: kh - pad, kw - pad, offset
+    float* s_decay = reinterpret_cast<float*>(s_tap + TKEYS);
     float* s_th = s_decay + p.decay_len;
     float* s_thx = s_th + p.T;
+    for (int i = threadIdx.x; i < TKEYS * CO; i += blockDim.x) {
+        const int f = i / CO, c = i - f * CO;
+        s_w[i] = (f < fan && c < p.C_out) ? p.W[f * p.C_out + c] : 0.0f;
+    }
+    for (int f = threadIdx.x; f < TKEYS; f += blockDim.x) {
+        const int tap = f / p.C_in, c = f - tap * p.C_in;
+        const int kh = tap / p.K, kw = tap - kh * p.K;
+        s_tap[f] = make_int4(kh - p.pad, kw - p.pad, (kh * p.W_in + kw) * p.C_in + c, 0);
+    }
     for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
-    const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
+    const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);   // ends with __syncthreads
     chain_wait();                                            // the input map is complete
 
     const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -40,18 +53,18 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     const long long r = pix / p.W_out;
     const int h_out = (int)(r % p.H_out);
     const long long img = r / p.H_out;
-    const int fan = p.K * p.K * p.C_in;
+    // input (kh, kw, c) sits at base + offset when its row and column are inside the map
+    const long long base = ((img * p.H_in + (h_out - p.pad)) * p.W_in + (w_out - p.pad)) * p.C_in;
 
     int key[TKEYS];
+    int n_ev = 0;
 #pragma unroll
     for (int f = 0; f < TKEYS; ++f) {
         key[f] = KEY_NONE;
         if (f < fan) {
-            const int tap = f / p.C_in, c = f - tap * p.C_in;
-            const int kh = tap / p.K, kw = tap - kh * p.K;
-            const int h_in = h_out - p.pad + kh, w_in = w_out - p.pad + kw;
-            if (h_in >= 0 && h_in < p.H_in && w_in >= 0 && w_in < p.W_in) {
-                const float t = __ldg(in + ((img * p.H_in + h_in) * p.W_in + w_in) * p.C_in + c);
+            const int4 tp = s_tap[f];
+            if ((unsigned)(h_out + tp.x) < (unsigned)p.H_in && (unsigned)(w_out + tp.y) < (unsigned)p.W_in) {
+                const float t = __ldg(in + (base + tp.z));
                 if (t < p.inf_time) {
                     int b = (int)floorf(t - p.tfs);
                     if (b < 0) b = 0;
@@ -64,6 +77,7 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
                             ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
                         }
                         key[f] = (b << 18) | (f << 13) | ti;
+                        ++n_ev;
                     }
                 }
             }
@@ -79,11 +93,11 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         nu.alive[c] = c < p.C_out;
     }
     int last = -1, cur = -1, next_t = 0;
-    while (nu.any()) {
+    for (int e = 0; e < n_ev && nu.any(); ++e) {
+        // the smallest key above the last one
         int m = KEY_NONE;
 #pragma unroll
-        for (int f = 0; f < TKEYS; ++f) m = (key[f] > last && key[f] < m) ? key[f] : m;
-        if (m == KEY_NONE) break;
+        for (int f = 0; f < TKEYS; ++f) m = min(m, key[f] > last ? key[f] : KEY_NONE);
         const int tb = m >> 18;
         if (tb != cur) {
             if (cur >= 0) {
@@ -94,10 +108,16 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
             cur = tb;
         }
         const float lv = s_decay[m & 0x1fff];
-        const float* wr = p.W + ((m >> 13) & 31) * p.C_out;
+        const float4* wr = reinterpret_cast<const float4*>(s_w + ((m >> 13) & 31) * CO);
 #pragma unroll
-        for (int c = 0; c < CO; ++c)
-            if (c < p.C_out) nu.acc[c] = fmaf(__ldg(wr + c), lv, nu.acc[c]);
+        for (int q = 0; q < CO / 4; ++q) {
+            const float4 w4 = wr[q];
+            const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+            float a[4] = {nu.acc[4 * q], nu.acc[4 * q + 1], nu.acc[4 * q + 2], nu.acc[4 * q + 3]};
+            fma_lanes<4>(a, w, lv);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) nu.acc[4 * q + j] = a[j];
+        }
         last = m;
     }
     if (cur >= 0 && nu.any()) {
@@ -112,9 +132,13 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         if (c < p.C_out) o[c] = nu.res[c];
 }
 
+size_t thread_smem(int CO, int T, int decay_len) {
+    return (size_t)TKEYS * CO * sizeof(float) + TKEYS * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
+}
+
 template <int CO>
 cudaError_t launch_thread_c(const IntegParams& p, const float* in, cudaStream_t s, long long n_pix) {
-    const size_t smem = (size_t)(p.decay_len + 2 * p.T) * sizeof(float);
+    const size_t smem = thread_smem(CO, p.T, p.decay_len);
     constexpr int REGS = TKEYS + 4 * CO + 40;
     constexpr int MINB = (65536 / (TW * 32 * REGS)) > 8 ? 8 : (65536 / (TW * 32 * REGS));
     auto kern = k_thread<CO, MINB>;
@@ -128,7 +152,7 @@ cudaError_t launch_thread_c(const IntegParams& p, const float* in, cudaStream_t 
 bool thread_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len) {
     if (is_fc || K * K * C_in > TKEYS || C_out > 16) return false;
     if (T >= (1 << 13)) return false;                          // 13-bit step / LUT index in the key
-    return (size_t)(decay_len + 2 * T) * sizeof(float) <= 48 * 1024;
+    return thread_smem(16, T, decay_len) <= 48 * 1024;
 }
 
 cudaError_t launch_thread(const IntegParams& p, const float* in, cudaStream_t s) {
