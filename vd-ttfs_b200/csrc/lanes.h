@@ -282,22 +282,32 @@ __device__ __forceinline__ void stream_block_sa(L& nu, unsigned sa, const float*
 // Stream step-sorted records through their runs: runs[j] = {end index of
 // run j in rec, its step}, runs in increasing step order, the records of one
 // run in FMA-chain order.  Full blocks of FS records run without any test;
-// a run's tail is split into blocks of 4, 2 and 1.  Each run ends with the
+// a run's tail is one block of its exact size, reached by a switch (one
+// indexed jump instead of a test per power-of-two piece).  Each run ends with the
 // close of its step (input-free steps before it are closed first).  Returns
 // false once every neuron of the warp has fired (the caller may stop).
 template <int V, int FS, class L, class TT>
 __device__ __forceinline__ bool stream_runs(L& nu, const int2* rec, int k, const int2* runs,
                                             int nruns, const float* Wl, int& next_t,
                                             const TT& tt) {
-    static_assert(FS == 4 || FS == 8, "a run's tail is covered by blocks of 4, 2 and 1");
+    static_assert(FS >= 1 && FS <= 8, "a run's tail (< FS records) is covered by blocks of 1 to 7");
     const unsigned sa0 = (unsigned)__cvta_generic_to_shared(rec);
     for (int j = 0; j < nruns; ++j) {
         const int2 rn = runs[j];
         const int end = rn.x;
         for (; k + FS <= end; k += FS) stream_block_sa<V, FS>(nu, sa0 + 8u * k, Wl);
-        if (end - k >= 4) { stream_block_sa<V, 4>(nu, sa0 + 8u * k, Wl); k += 4; }
-        if (end - k >= 2) { stream_block_sa<V, 2>(nu, sa0 + 8u * k, Wl); k += 2; }
-        if (end - k >= 1) { stream_block_sa<V, 1>(nu, sa0 + 8u * k, Wl); k += 1; }
+        // the run's tail (fewer than FS records): one indexed jump to a block of that size
+        switch (end - k) {
+            case 7: stream_block_sa<V, 7>(nu, sa0 + 8u * k, Wl); break;
+            case 6: stream_block_sa<V, 6>(nu, sa0 + 8u * k, Wl); break;
+            case 5: stream_block_sa<V, 5>(nu, sa0 + 8u * k, Wl); break;
+            case 4: stream_block_sa<V, 4>(nu, sa0 + 8u * k, Wl); break;
+            case 3: stream_block_sa<V, 3>(nu, sa0 + 8u * k, Wl); break;
+            case 2: stream_block_sa<V, 2>(nu, sa0 + 8u * k, Wl); break;
+            case 1: stream_block_sa<V, 1>(nu, sa0 + 8u * k, Wl); break;
+            default: break;
+        }
+        k = end;
         nu.close_empty(next_t, rn.y, tt);
         nu.close_step_bf(rn.y, tt);
         next_t = rn.y + 1;
