@@ -110,3 +110,36 @@ def test_thread_kernel_rejected_where_unsupported(O, dev):
         assert ei.value.status == 5
     ctx.close()
     m.close()
+
+
+PAIR_CASES = [(1, 3), (7, 5), (16, 3), (17, 3), (10, 1)]
+
+
+@pytest.mark.parametrize("c_out,B", PAIR_CASES, ids=[f"cout{c}-B{b}" for c, b in PAIR_CASES])
+def test_dense_two_pixels_per_warp_bitexact(O, dev, c_out, B):
+    """k_dense with at most 16 output channels runs two pixels per warp
+    (k_dense_pair) outside counting passes: odd pixel counts (the last warp
+    holds one pixel), 1 to 16 channels, and 17 channels (one pixel per warp)
+    give the oracle's maps bit for bit, with and without counting."""
+    from vdttfs import engine as E, nets, synth
+    c, f = nets._conv, nets._fc
+    net = nets.NetSpec(
+        "pair", 7, 9, 8, (c(8, c_out, 3, nets.PAD_SAME), f(7 * 9 * c_out, 10, nets.OUT_VMEM)),
+        T=40, delta=8, tfs=40.0, lut_mode=nets.LUT_BY_TIN, decay_len=41,
+        readout=nets.READ_ARGMAX, tc_in=34.75016403198242, encoder=nets.ENC_LINEAR)
+    layers = synth.kaiming_layers(net, 1, gains=[1.6, 1.0])
+    img = synth.images(1, B, 7, 9, 8, 0.3, stream=11)
+    spikes = O.encode_linear(img, net.T)
+    ref = O.run_net(net, layers, spikes, keep=True)
+    assert 0.0 < np.mean(ref["maps"][0] < net.inf_time) < 1.0
+    m = E.Model(net, layers, lut_source=E.LUT_HOST_LIBM)
+    ctx = E.Context(m, B)
+    assert ctx.layer_kernels()[0] == E.KERNEL_DENSE
+    for counting in (False, True):
+        ctx.set_counting(counting)
+        maps, out, pred = ctx.trace(_t(spikes, dev))
+        _sync()
+        assert bits_equal(_np(maps[0]).reshape(-1), ref["maps"][0]), f"counting={counting}"
+        assert bits_equal(_np(out), ref["out"]) and np.array_equal(_np(pred), ref["pred"])
+    ctx.close()
+    m.close()

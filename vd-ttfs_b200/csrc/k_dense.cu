@@ -18,6 +18,10 @@
 //      The warp stops once all its neurons fired.
 // The fetched-synapse counter keeps the reference's chunk accounting (events
 // of every chunk a neuron entered alive).
+//
+// Layers with at most 16 output channels run k_dense_pair instead (outside
+// counting passes): two pixels per warp, sorted one after the other by the
+// whole warp, streamed by one half-warp each.
 #include "lanes.h"
 #include "vdt_internal.h"
 
@@ -44,34 +48,23 @@ __device__ __forceinline__ int tap_of(int f, int C_in, float inv) {
     return j;
 }
 
-template <int V, int R, int MINB, bool COUNT>
-__global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const float* __restrict__ in,
-                                                         int n_warps, int groups) {
-    extern __shared__ __align__(16) int sm[];
-    __shared__ int s_floor, s_mono;
-    chain_release();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntaps = p.is_fc ? 1 : p.K * p.K;
-    const int fan = ntaps * p.C_in;
-    const int words = dense_words(fan, p.T, ntaps);
-    int* wb = sm + warp * words;
+size_t dense_smem(int fan, int T, int ntaps, int decay_len, int P) {
+    return (size_t)DW * P * dense_words(fan, T, ntaps) * sizeof(int) + (size_t)(decay_len + 2 * T) * sizeof(float);
+}
+
+// Sort one output pixel's events into its region (whole warp): reads the
+// K*K*C_in input times, stable counting sort by step, records {element
+// offset of the weight row, LUT value} in s_list and the run table in
+// s_runs; s_bin[tb] ends as the end of step tb's run.  Returns the number of
+// runs (warp-uniform).
+template <int R>
+__device__ __forceinline__ int sort_pixel(const IntegParams& p, const float* __restrict__ in, unsigned pix,
+                                          int fan, int ntaps, int* wb, const float* s_decay) {
+    const int lane = threadIdx.x & 31;
     int2* s_list = reinterpret_cast<int2*>(wb);
     int* s_bin = wb + ((2 * fan + 3) & ~3);                  // [T + 1]
     long long* s_col = reinterpret_cast<long long*>(s_bin + ((p.T + 1 + 3) & ~3));
     int2* s_runs = reinterpret_cast<int2*>(reinterpret_cast<int*>(s_col) + ((2 * ntaps + 3) & ~3));
-    float* s_decay = reinterpret_cast<float*>(sm + DW * words);
-    float* s_th = s_decay + p.decay_len;
-    float* s_thx = s_th + p.T;
-    for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
-    const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
-    chain_wait();                                            // the input map is complete
-
-    const int gw = blockIdx.x * DW + warp;
-    if (gw >= n_warps) return;                               // warp-uniform
-    const unsigned pix = (unsigned)gw / (unsigned)groups;
-    const int grp = gw - (int)pix * groups;
-    const int c0 = (grp * 32 + lane) * V;
-    const bool lane_ok = c0 < p.C_out;
     int w_out = 0, h_out = 0;
     long long img = pix;
     if (!p.is_fc) {
@@ -167,7 +160,37 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
         __syncwarp();
     }
     // s_bin[tb] is now the end of step tb's run
-    const int nruns = compact_runs(s_bin, p.T, 0, s_runs);
+    return compact_runs(s_bin, p.T, 0, s_runs);
+}
+
+template <int V, int R, int MINB, bool COUNT>
+__global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const float* __restrict__ in,
+                                                         int n_warps, int groups) {
+    extern __shared__ __align__(16) int sm[];
+    __shared__ int s_floor, s_mono;
+    chain_release();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntaps = p.is_fc ? 1 : p.K * p.K;
+    const int fan = ntaps * p.C_in;
+    const int words = dense_words(fan, p.T, ntaps);
+    int* wb = sm + warp * words;
+    int2* s_list = reinterpret_cast<int2*>(wb);
+    int* s_bin = wb + ((2 * fan + 3) & ~3);                  // [T + 1]
+    int2* s_runs = reinterpret_cast<int2*>(s_bin + ((p.T + 1 + 3) & ~3) + ((2 * ntaps + 3) & ~3));
+    float* s_decay = reinterpret_cast<float*>(sm + DW * words);
+    float* s_th = s_decay + p.decay_len;
+    float* s_thx = s_th + p.T;
+    for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
+    const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
+    chain_wait();                                            // the input map is complete
+
+    const int gw = blockIdx.x * DW + warp;
+    if (gw >= n_warps) return;                               // warp-uniform
+    const unsigned pix = (unsigned)gw / (unsigned)groups;
+    const int grp = gw - (int)pix * groups;
+    const int c0 = (grp * 32 + lane) * V;
+    const bool lane_ok = c0 < p.C_out;
+    const int nruns = sort_pixel<R>(p, in, pix, fan, ntaps, wb, s_decay);
 
     // 3. stream the runs
     Lanes<V> nu;
@@ -207,6 +230,83 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
         if (lane == 0 && fetched) atomicAdd(p.fetched, fetched);
     }
     if (lane_ok) store_res<V>(p.out + (long long)pix * p.C_out + c0, nu.res);
+}
+
+// Two output pixels per warp for layers with at most 16 output channels
+// (a warp per pixel would leave half of its lanes idle): the whole warp
+// sorts both pixels, one after the other, into two shared regions
+// (sort_pixel), then lanes 0-15 stream the first pixel and lanes 16-31 the
+// second, one channel per lane, sharing each run's loop, close and vote
+// instructions (stream_runs_grouped).  Outside counting passes only.
+template <int R, int MINB>
+__global__ void __launch_bounds__(DW * 32, MINB) k_dense_pair(IntegParams p, const float* __restrict__ in,
+                                                              int n_warps, long long n_pix) {
+    extern __shared__ __align__(16) int sm[];
+    __shared__ int s_floor, s_mono;
+    chain_release();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntaps = p.is_fc ? 1 : p.K * p.K;
+    const int fan = ntaps * p.C_in;
+    const int words = dense_words(fan, p.T, ntaps);
+    float* s_decay = reinterpret_cast<float*>(sm + DW * 2 * words);
+    float* s_th = s_decay + p.decay_len;
+    float* s_thx = s_th + p.T;
+    for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
+    const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
+    chain_wait();                                            // the input map is complete
+
+    const int gw = blockIdx.x * DW + warp;
+    if (gw >= n_warps) return;                               // warp-uniform
+    int nr[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const long long pix = 2ll * gw + q;
+        nr[q] = pix < n_pix ? sort_pixel<R>(p, in, (unsigned)pix, fan, ntaps, sm + (warp * 2 + q) * words, s_decay)
+                            : 0;
+    }
+    const int g = lane >> 4;
+    const long long pix = 2ll * gw + g;
+    const int* wb = sm + (warp * 2 + g) * words;
+    const int2* s_list = reinterpret_cast<const int2*>(wb);
+    const int2* s_runs = reinterpret_cast<const int2*>(wb + ((2 * fan + 3) & ~3) + ((p.T + 1 + 3) & ~3) +
+                                                       ((2 * ntaps + 3) & ~3));
+    const int c0 = lane & 15;
+    const bool lane_ok = c0 < p.C_out && pix < n_pix;
+    Lanes<1> nu;
+    nu.init(p.bias, c0, lane_ok, p.inf_time);
+    const float* Wl = p.W + (lane_ok ? c0 : 0);
+    int next_t = 0;
+    if (stream_runs_grouped<1, FS>(nu, s_list, s_runs, g ? nr[1] : nr[0], max(nr[0], nr[1]), Wl, next_t, tt))
+        nu.close_empty(next_t, p.T, tt);
+    if (lane_ok) p.out[pix * p.C_out + c0] = nu.res[0];
+}
+
+template <int R>
+cudaError_t launch_pair_r(const IntegParams& p, const float* in, cudaStream_t s, long long pixels) {
+    const long long n_warps = (pixels + 1) / 2;
+    if (n_warps <= 0) return cudaSuccess;
+    if (n_warps >= (1ll << 31)) return cudaErrorInvalidValue;   // 32-bit work index
+    const int ntaps = p.is_fc ? 1 : p.K * p.K;
+    const size_t smem = dense_smem(ntaps * p.C_in, p.T, ntaps, p.decay_len, 2);
+    constexpr int REGS = FS + 2 * FS + 4 + R;
+    constexpr int MINB = (65536 / (DW * 32 * REGS)) > 8 ? 8 : (65536 / (DW * 32 * REGS));
+    auto kern = k_dense_pair<R, MINB>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    return launch_chain(kern, dim3((unsigned)((n_warps + DW - 1) / DW)), dim3(DW * 32), smem, s, p, in,
+                        (int)n_warps, pixels);
+}
+
+cudaError_t launch_pair(const IntegParams& p, const float* in, cudaStream_t s) {
+    const long long pixels = p.is_fc ? (long long)p.B : (long long)p.B * p.H_out * p.W_out;
+    const int w = ((p.is_fc ? 1 : p.K * p.K) * p.C_in + 31) / 32;
+    if (w <= 1) return launch_pair_r<1>(p, in, s, pixels);
+    if (w <= 4) return launch_pair_r<4>(p, in, s, pixels);
+    if (w <= 9) return launch_pair_r<9>(p, in, s, pixels);
+    if (w <= 18) return launch_pair_r<18>(p, in, s, pixels);
+    return launch_pair_r<DENSE_WIN>(p, in, s, pixels);
 }
 
 int pick_v_dense(int C_out) {
@@ -263,6 +363,9 @@ bool dense_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len
 }
 
 cudaError_t launch_dense(const IntegParams& p, const float* in, cudaStream_t s) {
+    const int ntaps = p.is_fc ? 1 : p.K * p.K;
+    if (!p.fetched && p.C_out <= 16 && dense_smem(ntaps * p.C_in, p.T, ntaps, p.decay_len, 2) <= 160 * 1024)
+        return launch_pair(p, in, s);
     switch (pick_v_dense(p.C_out)) {
         case 4: return launch_dense_v<4>(p, in, s);
         case 2: return launch_dense_v<2>(p, in, s);

@@ -279,38 +279,66 @@ __device__ __forceinline__ void stream_block_sa(L& nu, unsigned sa, const float*
     for (int u = 0; u < U; ++u) fma_lanes<V>(nu.acc, w[u], __int_as_float(e[u].y));
 }
 
+// The records [k, end) of one run: full blocks of FS records without any
+// test, then the tail (fewer than FS records) as one block of its exact
+// size, reached by a switch (one indexed jump instead of a test per
+// power-of-two piece).
+template <int V, int FS, class L>
+__device__ __forceinline__ void stream_run_records(L& nu, unsigned sa0, int k, int end, const float* Wl) {
+    static_assert(FS >= 1 && FS <= 8, "a run's tail (< FS records) is covered by blocks of 1 to 7");
+    for (; k + FS <= end; k += FS) stream_block_sa<V, FS>(nu, sa0 + 8u * k, Wl);
+    switch (end - k) {
+        case 7: stream_block_sa<V, 7>(nu, sa0 + 8u * k, Wl); break;
+        case 6: stream_block_sa<V, 6>(nu, sa0 + 8u * k, Wl); break;
+        case 5: stream_block_sa<V, 5>(nu, sa0 + 8u * k, Wl); break;
+        case 4: stream_block_sa<V, 4>(nu, sa0 + 8u * k, Wl); break;
+        case 3: stream_block_sa<V, 3>(nu, sa0 + 8u * k, Wl); break;
+        case 2: stream_block_sa<V, 2>(nu, sa0 + 8u * k, Wl); break;
+        case 1: stream_block_sa<V, 1>(nu, sa0 + 8u * k, Wl); break;
+        default: break;
+    }
+}
+
 // Stream step-sorted records through their runs: runs[j] = {end index of
 // run j in rec, its step}, runs in increasing step order, the records of one
-// run in FMA-chain order.  Full blocks of FS records run without any test;
-// a run's tail is one block of its exact size, reached by a switch (one
-// indexed jump instead of a test per power-of-two piece).  Each run ends with the
-// close of its step (input-free steps before it are closed first).  Returns
-// false once every neuron of the warp has fired (the caller may stop).
+// run in FMA-chain order.  Each run ends with the close of its step
+// (input-free steps before it are closed first).  Returns false once every
+// neuron of the warp has fired (the caller may stop).
 template <int V, int FS, class L, class TT>
 __device__ __forceinline__ bool stream_runs(L& nu, const int2* rec, int k, const int2* runs,
                                             int nruns, const float* Wl, int& next_t,
                                             const TT& tt) {
-    static_assert(FS >= 1 && FS <= 8, "a run's tail (< FS records) is covered by blocks of 1 to 7");
     const unsigned sa0 = (unsigned)__cvta_generic_to_shared(rec);
     for (int j = 0; j < nruns; ++j) {
         const int2 rn = runs[j];
-        const int end = rn.x;
-        for (; k + FS <= end; k += FS) stream_block_sa<V, FS>(nu, sa0 + 8u * k, Wl);
-        // the run's tail (fewer than FS records): one indexed jump to a block of that size
-        switch (end - k) {
-            case 7: stream_block_sa<V, 7>(nu, sa0 + 8u * k, Wl); break;
-            case 6: stream_block_sa<V, 6>(nu, sa0 + 8u * k, Wl); break;
-            case 5: stream_block_sa<V, 5>(nu, sa0 + 8u * k, Wl); break;
-            case 4: stream_block_sa<V, 4>(nu, sa0 + 8u * k, Wl); break;
-            case 3: stream_block_sa<V, 3>(nu, sa0 + 8u * k, Wl); break;
-            case 2: stream_block_sa<V, 2>(nu, sa0 + 8u * k, Wl); break;
-            case 1: stream_block_sa<V, 1>(nu, sa0 + 8u * k, Wl); break;
-            default: break;
-        }
-        k = end;
+        stream_run_records<V, FS>(nu, sa0, k, rn.x, Wl);
+        k = rn.x;
         nu.close_empty(next_t, rn.y, tt);
         nu.close_step_bf(rn.y, tt);
         next_t = rn.y + 1;
+        if (!__any_sync(FULL_MASK, nu.any())) return false;
+    }
+    return true;
+}
+
+// The same for several pixels per warp: each lane follows its own pixel's
+// records and runs (rec, runs, nruns differ between lane groups); jmax is
+// the warp's largest run count.  The groups share one pass of the run loop;
+// the all-fired vote is taken by the whole warp once per run index.
+template <int V, int FS, class L, class TT>
+__device__ __forceinline__ bool stream_runs_grouped(L& nu, const int2* rec, const int2* runs, int nruns,
+                                                    int jmax, const float* Wl, int& next_t, const TT& tt) {
+    const unsigned sa0 = (unsigned)__cvta_generic_to_shared(rec);
+    int k = 0;
+    for (int j = 0; j < jmax; ++j) {
+        if (j < nruns) {
+            const int2 rn = runs[j];
+            stream_run_records<V, FS>(nu, sa0, k, rn.x, Wl);
+            k = rn.x;
+            nu.close_empty(next_t, rn.y, tt);
+            nu.close_step_bf(rn.y, tt);
+            next_t = rn.y + 1;
+        }
         if (!__any_sync(FULL_MASK, nu.any())) return false;
     }
     return true;
