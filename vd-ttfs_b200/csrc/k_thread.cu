@@ -7,10 +7,11 @@
 // layer would leave 26 of 32 lanes idle.  The thread reads its pixel's inputs
 // once into registers as keys (step << 18 | input index << 13 | LUT index), so
 // increasing key order is the reference's order: by step, and inside a step
-// by (tap, channel) -- each neuron's FMA chain.  The thread then repeatedly
-// takes the smallest key above the last one (a min over its registers), adds
-// w[input][c] * LUT to every channel's open step, and closes a step when the
-// next key leaves it (lanes.h closes; input-free steps by bisection).
+// by (tap, channel) -- each neuron's FMA chain.  A bitonic network sorts the
+// keys in registers once; the thread then walks its sorted events from its
+// own shared-memory column, adds w[input][c] * LUT to every channel's open
+// step, and closes a step when the next key leaves it (lanes.h closes;
+// input-free steps by bisection).
 #include "lanes.h"
 #include "vdt_internal.h"
 
@@ -20,6 +21,27 @@ namespace {
 constexpr int TW = 4;             // warps per CTA
 constexpr int TKEYS = 32;         // inputs per pixel held in registers
 constexpr int KEY_NONE = 0x7fffffff;
+
+// ascending bitonic sort of N keys held in registers (N a power of two;
+// fully unrolled, so every compare-exchange is one min and one max)
+template <int N>
+__device__ __forceinline__ void sort_keys(int (&k)[N]) {
+#pragma unroll
+    for (int size = 2; size <= N; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+            for (int i = 0; i < N; ++i) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const int a = k[i], b = k[j];
+                    const int lo = min(a, b), hi = max(a, b);
+                    if ((i & size) == 0) { k[i] = lo; k[j] = hi; } else { k[i] = hi; k[j] = lo; }
+                }
+            }
+        }
+    }
+}
 
 template <int CO, int MINB>
 __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const float* __restrict__ in,
@@ -31,7 +53,8 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     // weights padded to CO columns (zeros past C_out), one row per input
     float* s_w = tsm;                                        // [TKEYS][CO]
     int4* s_tap = reinterpret_cast<int4*>(s_w + TKEYS * CO); // per input: kh - pad, kw - pad, offset
-    float* s_decay = reinterpret_cast<float*>(s_tap + TKEYS);
+    int* s_keys = reinterpret_cast<int*>(s_tap + TKEYS);    // [TKEYS][TW * 32]: a column per thread
+    float* s_decay = reinterpret_cast<float*>(s_keys + TKEYS * TW * 32);
     float* s_th = s_decay + p.decay_len;
     float* s_thx = s_th + p.T;
     for (int i = threadIdx.x; i < TKEYS * CO; i += blockDim.x) {
@@ -84,6 +107,13 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         }
     }
 
+    // sorted once (keys are distinct: the input index is part of each), the
+    // events first; staged in the thread's own shared-memory column
+    sort_keys<TKEYS>(key);
+#pragma unroll
+    for (int e = 0; e < TKEYS; ++e)
+        if (e < n_ev) s_keys[e * (TW * 32) + threadIdx.x] = key[e];
+
     Lanes<CO> nu;
 #pragma unroll
     for (int c = 0; c < CO; ++c) {
@@ -92,12 +122,9 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         nu.acc[c] = 0.0f;
         nu.alive[c] = c < p.C_out;
     }
-    int last = -1, cur = -1, next_t = 0;
+    int cur = -1, next_t = 0;
     for (int e = 0; e < n_ev && nu.any(); ++e) {
-        // the smallest key above the last one
-        int m = KEY_NONE;
-#pragma unroll
-        for (int f = 0; f < TKEYS; ++f) m = min(m, key[f] > last ? key[f] : KEY_NONE);
+        const int m = s_keys[e * (TW * 32) + threadIdx.x];
         const int tb = m >> 18;
         if (tb != cur) {
             if (cur >= 0) {
@@ -118,7 +145,6 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
 #pragma unroll
             for (int j = 0; j < 4; ++j) nu.acc[4 * q + j] = a[j];
         }
-        last = m;
     }
     if (cur >= 0 && nu.any()) {
         nu.close_empty(next_t, cur, tt);
@@ -133,13 +159,14 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
 }
 
 size_t thread_smem(int CO, int T, int decay_len) {
-    return (size_t)TKEYS * CO * sizeof(float) + TKEYS * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
+    return (size_t)TKEYS * CO * sizeof(float) + TKEYS * sizeof(int4) + (size_t)TKEYS * TW * 32 * sizeof(int) +
+           (size_t)(decay_len + 2 * T) * sizeof(float);
 }
 
 template <int CO>
 cudaError_t launch_thread_c(const IntegParams& p, const float* in, cudaStream_t s, long long n_pix) {
     const size_t smem = thread_smem(CO, p.T, p.decay_len);
-    constexpr int REGS = TKEYS + 4 * CO + 40;
+    constexpr int REGS = CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO;   // keys + lane state
     constexpr int MINB = (65536 / (TW * 32 * REGS)) > 8 ? 8 : (65536 / (TW * 32 * REGS));
     auto kern = k_thread<CO, MINB>;
     const long long blocks = (n_pix + TW * 32 - 1) / (TW * 32);
