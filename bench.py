@@ -445,14 +445,19 @@ def dvs_stages(dvs, spec, w, x, N, marks=None):
         return r
 
     spec0, spec = spec, dvs.internal_spec(spec)
+    def conv(name, y, wt, cin, cout, h, wd):
+        # the fused kernel (bucketing inside the conv) where it applies, as dvs.run
+        if dvs.dense_supported(cin, spec.k):
+            ev[name] = None
+            return mark(name, lambda: dvs.conv_dense(y, wt, N, cin, cout, h, wd, spec))
+        b = mark("bucketize", lambda: dvs.bucketize_sites(y, N, cin, h, wd, spec))
+        ev[name] = b
+        return mark(name, lambda: dvs.conv_bucketed(b, wt, N, cin, cout, h, wd, spec))
+
     y = mark("conv1_raw", lambda: dvs.conv1_raw(x, w.conv1, spec0))
-    b = mark("bucketize", lambda: dvs.bucketize_sites(y, N, c1n, H, W, spec))
-    ev["conv2"] = b
-    y = mark("conv2", lambda: dvs.conv_bucketed(b, w.conv2, N, c1n, c2n, H, W, spec))
+    y = conv("conv2", y, w.conv2, c1n, c2n, H, W)
     y = mark("pool1", lambda: dvs.pool(y, N, c2n, H, W, spec))
-    b = mark("bucketize", lambda: dvs.bucketize_sites(y, N, c2n, H2, W2, spec))
-    ev["conv3"] = b
-    y = mark("conv3", lambda: dvs.conv_bucketed(b, w.conv3, N, c2n, c3n, H2, W2, spec))
+    y = conv("conv3", y, w.conv3, c2n, c3n, H2, W2)
     y = mark("pool2", lambda: dvs.pool(y, N, c3n, H2, W2, spec))
     b = mark("bucketize", lambda: dvs.bucketize_rows(y, N, s["fc1_in"], spec))
     ev["fc1"] = b
@@ -468,14 +473,15 @@ def dvs_stages(dvs, spec, w, x, N, marks=None):
 def dvs_bytes(spec, N, ev):
     """Algorithmic bytes of one DVS batch: every stage's input map read and
     output map written once (conv1: the dense frames), the bucketed stages'
-    lists written and read back (8 B per kept event, 4 B per chunk offset),
-    the weights once."""
+    lists written and read back (8 B per kept event, 4 B per chunk offset;
+    none for a conv that reads its input map itself), the weights once."""
     s = spec.stage_shapes()
     c1n, c2n, c3n = spec.convs
     HW, HW2, HW4 = spec.H * spec.W, spec.H * spec.W // 4, spec.H * spec.W // 16
     OS = spec.n_chunks + 1
     k2 = spec.k * spec.k
-    lists = lambda name, cols: 2 * (8 * int(ev[name][0][:, -1].sum().item()) + 4 * cols * OS)
+    # a fused conv (ev[name] None) writes and reads no lists
+    lists = lambda name, cols: 0 if ev[name] is None else 2 * (8 * int(ev[name][0][:, -1].sum().item()) + 4 * cols * OS)
     b = 4 * N * spec.in_c * HW * spec.T + 4 * N * c1n * HW + 4 * c1n * spec.in_c * k2          # conv1
     b += 4 * N * c1n * HW + 4 * N * c2n * HW + lists("conv2", N * HW) + 4 * c2n * c1n * k2    # conv2
     b += 4 * N * c2n * HW + 4 * N * c2n * HW2                                                    # pool1

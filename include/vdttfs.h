@@ -253,6 +253,17 @@ int vdt_dvs_conv_bucketed(const int* d_off, const int* d_cin, const float* d_tin
                           int T, int delta, float decay, float th, int out_layout, float* d_out,
                           vdt_stream stream);
 
+/* k_bucketize_conv (t3:70-90) and conv_bucketed_early (t3:109-143) in one
+   launch: reads the layer's input spike map (d_in, NCHW or NHWC per
+   in_layout) instead of bucket lists, same results as
+   vdt_bucketize (VDT_TB_TRUNC) + vdt_dvs_conv_bucketed bit for bit (each
+   step's input summed in (ky, kx, channel) order, every step scanned up to
+   ceil(T / delta) * delta).  VDT_ERR_UNSUPPORTED unless K*K*C_in <= 1152
+   and K*K <= 32. */
+int vdt_dvs_conv_dense(const float* d_in, int in_layout, const float* d_w_hwio, int N, int C_in, int C_out,
+                       int H, int W, int K, int T, int delta, float decay, float th, int out_layout,
+                       float* d_out, vdt_stream stream);
+
 /* pool_chunk_early (t3:146-168): spiking 2x2 pool, in[t] = 1 at each input
    spike's bin; layout VDT_LAYOUT_NCHW or VDT_LAYOUT_NHWC (in and out). */
 int vdt_dvs_pool(const float* d_in, float* d_out, int N, int C, int H_in, int W_in, int layout,

@@ -70,6 +70,47 @@ def test_conv_bucketed_early_every_delta(O, dev, delta):
     assert bits_equal(nhwc, ref)
 
 
+DENSE_CASES = [(8, 160, 48, 96), (32, 160, 128, 64), (32, 150, 48, 96), (16, 77, 3, 40), (64, 160, 20, 128)]
+
+
+@pytest.mark.parametrize("delta,T,C_in,C_out", DENSE_CASES, ids=[f"d{c[0]}-T{c[1]}-cin{c[2]}" for c in DENSE_CASES])
+def test_conv_dense_equals_bucketed(O, dev, delta, T, C_in, C_out):
+    """vdt_dvs_conv_dense (bucketing fused into the CuLIF conv, reading the
+    spike map) gives conv_bucketed_early's result bit for bit: NCHW and NHWC
+    input and output, fan-in up to 1152, T not a multiple of delta (the scan
+    runs past T to the end of the last chunk, as the reference's)."""
+    from vdttfs import dvs, nets
+    spec = nets.dvs_ref(T=T, delta=delta)
+    rng = np.random.default_rng(delta * 1000 + C_in)
+    N, H, W = 2, 9, 7
+    x = spike_map(rng, (N, C_in, H, W), fire=0.35, T=spec.T, edges=True)
+    w = (rng.standard_normal((C_out, C_in, 3, 3)) * np.float32(0.35 * np.sqrt(48.0 / C_in))).astype(np.float32)
+    off, cin, tin, _ = O.bucketize(x, N * H * W, C_in, spec.T, delta, 0.0, 1, 1, H * W)
+    ref = np.empty(N * C_out * H * W, np.float32)
+    O.lib().orc_dvs_conv(O._i(off), O._i(cin), O._f(tin), O._f(w), N, C_in, C_out, H, W, 3, spec.T, delta,
+                         spec.decay_conv, spec.th_conv, O._f(ref))
+    assert 0.0 < np.mean(ref < INF) < 1.0
+    wd = dvs.oihw_to_hwio(_t(w, dev))
+    assert dvs.dense_supported(C_in, 3)
+    got = _np(dvs.conv_dense(_t(x, dev), wd, N, C_in, C_out, H, W, spec))
+    assert bits_equal(got, ref), f"{np.sum(got != ref)} of {ref.size} differ"
+    xh = np.ascontiguousarray(x.transpose(0, 2, 3, 1))
+    got2 = _np(dvs.conv_dense(_t(xh, dev), wd, N, C_in, C_out, H, W, spec, in_layout=0, out_layout=0))
+    assert bits_equal(got2.reshape(N, H, W, C_out).transpose(0, 3, 1, 2).reshape(-1), ref)
+
+
+def test_conv_dense_rejects_large_fan_in(dev):
+    from vdttfs import dvs, engine as E, nets
+    import torch
+    spec = nets.dvs_ref()
+    assert not dvs.dense_supported(129, 3)
+    x = torch.full((1 * 129 * 4 * 4,), INF, device=dev)
+    w = torch.zeros((3, 3, 129, 8), device=dev)
+    with pytest.raises(E.VdtError) as ei:
+        dvs.conv_dense(x, w, 1, 129, 8, 4, 4, spec)
+    assert ei.value.status == 5
+
+
 @pytest.mark.parametrize("layout", [0, 1])
 def test_pool_chunk_early(O, dev, layout):
     from vdttfs import dvs, nets

@@ -52,6 +52,30 @@ extern "C" int vdt_dvs_conv_bucketed(const int* d_off, const int* d_cin, const f
     return cuda_status(launch_culif(ip, static_cast<cudaStream_t>(stream)), "conv_bucketed_early launch");
 }
 
+extern "C" int vdt_dvs_conv_dense(const float* d_in, int in_layout, const float* d_w_hwio, int N, int C_in,
+                                  int C_out, int H, int W, int K, int T, int delta, float decay, float th,
+                                  int out_layout, float* d_out, vdt_stream stream) {
+    api_clear_error();
+    if (!d_in || !d_w_hwio || !d_out || N < 0 || C_in <= 0 || C_out <= 0 || H <= 0 || W <= 0 || K <= 0 ||
+        K % 2 == 0 || !culif_ok(T, delta))
+        return api_fail(VDT_ERR_INVALID, "bad conv_dense arguments");
+    if ((in_layout != VDT_LAYOUT_NHWC && in_layout != VDT_LAYOUT_NCHW) ||
+        (out_layout != VDT_LAYOUT_NHWC && out_layout != VDT_LAYOUT_NCHW))
+        return api_fail(VDT_ERR_INVALID, "in_layout / out_layout");
+    if (!dense_supported(K, 0, C_in, C_out, T, 0))
+        return api_fail(VDT_ERR_UNSUPPORTED, "conv_dense needs K*K*C_in <= 1152 and K*K <= 32");
+    if (int s = api_check_buffers(-1, {d_in, d_w_hwio, d_out})) return s;
+    IntegParams ip{};
+    ip.W = d_w_hwio; ip.out = d_out;
+    ip.B = N; ip.H_in = H; ip.W_in = W; ip.C_in = C_in; ip.H_out = H; ip.W_out = W; ip.C_out = C_out;
+    ip.K = K; ip.pad = K / 2; ip.is_fc = 0;
+    ip.T = T; ip.delta = delta; ip.NC = (T + delta - 1) / delta;
+    ip.inf_time = 9999.0f; ip.culif_decay = decay; ip.culif_th = th;
+    ip.out_nchw = out_layout == VDT_LAYOUT_NCHW;
+    ip.in_nchw = in_layout == VDT_LAYOUT_NCHW;
+    return cuda_status(launch_dense_culif(ip, d_in, static_cast<cudaStream_t>(stream)), "conv_dense launch");
+}
+
 extern "C" int vdt_dvs_fc2(const int* d_off, const int* d_cin, const float* d_tin, const float* d_w_t, int N,
                            int F_in, int F_out, int T, int delta, float decay, float th, float* d_out,
                            vdt_stream stream) {

@@ -22,6 +22,8 @@
 // Layers with at most 16 output channels run k_dense_pair instead (outside
 // counting passes): two pixels per warp, sorted one after the other by the
 // whole warp, streamed by one half-warp each.
+#include <type_traits>
+
 #include "lanes.h"
 #include "vdt_internal.h"
 
@@ -57,7 +59,10 @@ size_t dense_smem(int fan, int T, int ntaps, int decay_len, int P) {
 // offset of the weight row, LUT value} in s_list and the run table in
 // s_runs; s_bin[tb] ends as the end of step tb's run.  Returns the number of
 // runs (warp-uniform).
-template <int R>
+// CULIF: the task-3 rule (tb = (int)t, kept iff 0 <= tb < T, t3:79; the
+// record's LUT value is 1, so the chain adds the weight exactly) and the
+// input map may be NCHW (p.in_nchw).
+template <int R, bool CULIF>
 __device__ __forceinline__ int sort_pixel(const IntegParams& p, const float* __restrict__ in, unsigned pix,
                                           int fan, int ntaps, int* wb, const float* s_decay) {
     const int lane = threadIdx.x & 31;
@@ -77,18 +82,22 @@ __device__ __forceinline__ int sort_pixel(const IntegParams& p, const float* __r
     if (lane < ntaps) {
         long long col = -1;
         if (p.is_fc) {
-            col = img;
+            col = img * p.C_in;                              // one column of C_in features
         } else {
             const int kh = lane / p.K, kw = lane - (lane / p.K) * p.K;
             const int h_in = h_out - p.pad + kh, w_in = w_out - p.pad + kw;
-            if (h_in >= 0 && h_in < p.H_in && w_in >= 0 && w_in < p.W_in)
-                col = (img * p.H_in + h_in) * p.W_in + w_in;
+            if (h_in >= 0 && h_in < p.H_in && w_in >= 0 && w_in < p.W_in) {
+                if (CULIF && p.in_nchw) col = ((img * p.C_in) * p.H_in + h_in) * p.W_in + w_in;
+                else col = ((img * p.H_in + h_in) * p.W_in + w_in) * p.C_in;
+            }
         }
-        s_col[lane] = col < 0 ? -1 : col * p.C_in;
+        s_col[lane] = col;
     }
     for (int i = lane; i <= p.T; i += 32) s_bin[i] = 0;
     __syncwarp();
 
+    // channel stride of the input map: 1 (NHWC) or H*W (NCHW, CuLIF layers)
+    const long long cs = (CULIF && p.in_nchw) ? (long long)p.H_in * p.W_in : 1;
     const float inv = 1.0f / (float)p.C_in;
     const unsigned lt = (1u << lane) - 1u;
     // all of the pixel's inputs in one round trip: input f = r*32 + lane
@@ -100,7 +109,7 @@ __device__ __forceinline__ int sort_pixel(const IntegParams& p, const float* __r
         if (f < fan) {
             const int j = tap_of(f, p.C_in, inv);
             const long long cb = s_col[j];
-            if (cb >= 0) tv[r] = __ldg(in + cb + (f - j * p.C_in));
+            if (cb >= 0) tv[r] = __ldg(in + cb + (f - j * p.C_in) * cs);
         }
     }
     // input value -> key = tb | LUT index << 16 (bucketize rule), -1 if no event
@@ -109,7 +118,12 @@ __device__ __forceinline__ int sort_pixel(const IntegParams& p, const float* __r
     for (int r = 0; r < R; ++r) {
         const float t = tv[r];
         key[r] = -1;
-        if (t < p.inf_time) {
+        if constexpr (CULIF) {
+            if (t < p.inf_time) {
+                const int b = (int)t;
+                if (b >= 0 && b < p.T) key[r] = b;
+            }
+        } else if (t < p.inf_time) {
             int b = (int)floorf(t - p.tfs);
             if (b < 0) b = 0;
             if (b < p.T) {
@@ -154,7 +168,8 @@ __device__ __forceinline__ int sort_pixel(const IntegParams& p, const float* __r
         if (tb >= 0) pos = s_bin[tb] + __popc(g & lt);
         __syncwarp();
         if (tb >= 0) {
-            s_list[pos] = make_int2((r * 32 + lane) * p.C_out, __float_as_int(s_decay[key[r] >> 16]));
+            s_list[pos] = make_int2((r * 32 + lane) * p.C_out,
+                                    CULIF ? __float_as_int(1.0f) : __float_as_int(s_decay[key[r] >> 16]));
             if (lane == __ffs(g) - 1) s_bin[tb] += __popc(g);
         }
         __syncwarp();
@@ -163,9 +178,13 @@ __device__ __forceinline__ int sort_pixel(const IntegParams& p, const float* __r
     return compact_runs(s_bin, p.T, 0, s_runs);
 }
 
-template <int V, int R, int MINB, bool COUNT>
+// CULIF: the task-3 conv_bucketed_early neuron (t3:109-143) fed straight
+// from the spike map: CulifLanes, every step scanned up to NC * delta (the
+// reference scans whole chunks), output NHWC or NCHW (p.out_nchw).
+template <int V, int R, int MINB, bool COUNT, bool CULIF>
 __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const float* __restrict__ in,
                                                          int n_warps, int groups) {
+    static_assert(!(COUNT && CULIF), "no counters on CuLIF layers");
     extern __shared__ __align__(16) int sm[];
     __shared__ int s_floor, s_mono;
     chain_release();
@@ -180,8 +199,12 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
     float* s_decay = reinterpret_cast<float*>(sm + DW * words);
     float* s_th = s_decay + p.decay_len;
     float* s_thx = s_th + p.T;
-    for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
-    const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
+    ThTables tt{};
+    if constexpr (!CULIF) {
+        for (int i = threadIdx.x; i < p.decay_len; i += blockDim.x) s_decay[i] = p.lut_decay[i];
+        tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);
+    }
+    const CulifCfg cc{p.culif_decay, p.culif_th};
     chain_wait();                                            // the input map is complete
 
     const int gw = blockIdx.x * DW + warp;
@@ -190,14 +213,26 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
     const int grp = gw - (int)pix * groups;
     const int c0 = (grp * 32 + lane) * V;
     const bool lane_ok = c0 < p.C_out;
-    const int nruns = sort_pixel<R>(p, in, pix, fan, ntaps, wb, s_decay);
+    const int nruns = sort_pixel<R, CULIF>(p, in, pix, fan, ntaps, wb, s_decay);
 
     // 3. stream the runs
-    Lanes<V> nu;
-    nu.init(p.bias, c0, lane_ok, p.inf_time);
+    std::conditional_t<CULIF, CulifLanes<V>, Lanes<V>> nu;
+    if constexpr (CULIF) nu.init(lane_ok, p.inf_time);
+    else nu.init(p.bias, c0, lane_ok, p.inf_time);
     const float* Wl = p.W + (lane_ok ? c0 : 0);
     int next_t = 0;
-    if constexpr (!COUNT) {
+    if constexpr (CULIF) {
+        if (stream_runs<V, FS>(nu, s_list, 0, s_runs, nruns, Wl, next_t, cc))
+            nu.close_empty(next_t, p.NC * p.delta, cc);
+        if (lane_ok && p.out_nchw) {
+            const unsigned r = pix / (unsigned)p.W_out, q = r / (unsigned)p.H_out;
+            const long long plane = (long long)p.H_out * p.W_out;
+            const long long site = (long long)(r - q * (unsigned)p.H_out) * p.W_out + (pix - r * (unsigned)p.W_out);
+#pragma unroll
+            for (int v = 0; v < V; ++v) p.out[((long long)q * p.C_out + c0 + v) * plane + site] = nu.res[v];
+            return;
+        }
+    } else if constexpr (!COUNT) {
         if (stream_runs<V, FS>(nu, s_list, 0, s_runs, nruns, Wl, next_t, tt))
             nu.close_empty(next_t, p.T, tt);
     } else {
@@ -261,7 +296,7 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense_pair(IntegParams p, con
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
         const long long pix = 2ll * gw + q;
-        nr[q] = pix < n_pix ? sort_pixel<R>(p, in, (unsigned)pix, fan, ntaps, sm + (warp * 2 + q) * words, s_decay)
+        nr[q] = pix < n_pix ? sort_pixel<R, false>(p, in, (unsigned)pix, fan, ntaps, sm + (warp * 2 + q) * words, s_decay)
                             : 0;
     }
     const int g = lane >> 4;
@@ -315,7 +350,7 @@ int pick_v_dense(int C_out) {
     return 1;
 }
 
-template <int V, int R>
+template <int V, int R, bool CULIF>
 cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t s, int n_warps,
                             int groups) {
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
@@ -323,9 +358,10 @@ cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t 
                         (size_t)(p.decay_len + 2 * p.T) * sizeof(float);
     // register budget tuned for occupancy (the kernel is latency-bound): the
     // streamed block, lane state and the sort's input registers
-    constexpr int REGS = FS * V + 2 * FS + 4 * V + R;
+    constexpr int REGS = FS * V + 2 * FS + (CULIF ? 5 : 4) * V + R;
     constexpr int MINB = (65536 / (DW * 32 * REGS)) > 8 ? 8 : (65536 / (DW * 32 * REGS));
-    auto kern = p.fetched ? k_dense<V, R, MINB, true> : k_dense<V, R, MINB, false>;
+    auto kern = CULIF ? k_dense<V, R, MINB, false, true>
+                      : (p.fetched ? k_dense<V, R, MINB, true, false> : k_dense<V, R, MINB, false, false>);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
@@ -333,7 +369,7 @@ cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t 
     return launch_chain(kern, dim3((n_warps + DW - 1) / DW), dim3(DW * 32), smem, s, p, in, n_warps, groups);
 }
 
-template <int V>
+template <int V, bool CULIF>
 cudaError_t launch_dense_v(const IntegParams& p, const float* in, cudaStream_t s) {
     const int groups = (p.C_out + 32 * V - 1) / (32 * V);
     const long long pixels = p.is_fc ? (long long)p.B : (long long)p.B * p.H_out * p.W_out;
@@ -343,11 +379,11 @@ cudaError_t launch_dense_v(const IntegParams& p, const float* in, cudaStream_t s
     const int nw = (int)n_warps;
     const int fan = (p.is_fc ? 1 : p.K * p.K) * p.C_in;
     const int w = (fan + 31) / 32;                          // 32-input windows per pixel
-    if (w <= 1) return launch_dense_vr<V, 1>(p, in, s, nw, groups);
-    if (w <= 4) return launch_dense_vr<V, 4>(p, in, s, nw, groups);
-    if (w <= 9) return launch_dense_vr<V, 9>(p, in, s, nw, groups);
-    if (w <= 18) return launch_dense_vr<V, 18>(p, in, s, nw, groups);
-    return launch_dense_vr<V, DENSE_WIN>(p, in, s, nw, groups);
+    if (w <= 1) return launch_dense_vr<V, 1, CULIF>(p, in, s, nw, groups);
+    if (w <= 4) return launch_dense_vr<V, 4, CULIF>(p, in, s, nw, groups);
+    if (w <= 9) return launch_dense_vr<V, 9, CULIF>(p, in, s, nw, groups);
+    if (w <= 18) return launch_dense_vr<V, 18, CULIF>(p, in, s, nw, groups);
+    return launch_dense_vr<V, DENSE_WIN, CULIF>(p, in, s, nw, groups);
 }
 
 }  // namespace
@@ -367,9 +403,17 @@ cudaError_t launch_dense(const IntegParams& p, const float* in, cudaStream_t s) 
     if (!p.fetched && p.C_out <= 16 && dense_smem(ntaps * p.C_in, p.T, ntaps, p.decay_len, 2) <= 160 * 1024)
         return launch_pair(p, in, s);
     switch (pick_v_dense(p.C_out)) {
-        case 4: return launch_dense_v<4>(p, in, s);
-        case 2: return launch_dense_v<2>(p, in, s);
-        default: return launch_dense_v<1>(p, in, s);
+        case 4: return launch_dense_v<4, false>(p, in, s);
+        case 2: return launch_dense_v<2, false>(p, in, s);
+        default: return launch_dense_v<1, false>(p, in, s);
+    }
+}
+
+cudaError_t launch_dense_culif(const IntegParams& p, const float* in, cudaStream_t s) {
+    switch (pick_v_dense(p.C_out)) {
+        case 4: return launch_dense_v<4, true>(p, in, s);
+        case 2: return launch_dense_v<2, true>(p, in, s);
+        default: return launch_dense_v<1, true>(p, in, s);
     }
 }
 

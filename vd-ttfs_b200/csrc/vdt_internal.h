@@ -85,6 +85,7 @@ struct IntegParams {
     // out_nchw = 1 writes the output map NCHW [B, C_out, H_out, W_out]
     float culif_decay, culif_th;
     int out_nchw;
+    int in_nchw;   // launch_dense_culif: the input spike map is NCHW [B, C_in, H_in, W_in]
 };
 cudaError_t launch_integrate(const IntegParams& p, cudaStream_t s);
 // true when launch_integrate supports this (K, delta, C_out) combination
@@ -94,6 +95,10 @@ bool integrate_supported(int K, int is_fc, int delta, int C_out, int T, int deca
 // NHWC spike map `in` directly (same results as bucketize + integrate).
 cudaError_t launch_dense(const IntegParams& p, const float* in, cudaStream_t s);
 bool dense_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len);
+// The same for task-3 CuLIF conv layers (conv_bucketed_early t3:109-143 fused
+// with its k_bucketize_conv, t3:70-89): reads the spike map (NHWC or NCHW),
+// scans every step up to NC * delta.  Supported where dense_supported is.
+cudaError_t launch_dense_culif(const IntegParams& p, const float* in, cudaStream_t s);
 
 // One thread per output pixel for narrow conv layers (K*K*C_in <= 32,
 // C_out <= 16): reads the NHWC spike map directly, same results.

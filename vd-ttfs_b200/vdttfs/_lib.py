@@ -77,6 +77,8 @@ SIGNATURES = {
     "vdt_dvs_conv1_raw": (C.c_int, [_vp, _vp] + [C.c_int] * 8 + [C.c_float, C.c_float, _vp, _vp]),
     "vdt_dvs_conv_bucketed": (C.c_int, [_vp, _vp, _vp, _vp] + [C.c_int] * 8 +
                               [C.c_float, C.c_float, C.c_int, _vp, _vp]),
+    "vdt_dvs_conv_dense": (C.c_int, [_vp, C.c_int, _vp] + [C.c_int] * 8 +
+                           [C.c_float, C.c_float, C.c_int, _vp, _vp]),
     "vdt_dvs_pool": (C.c_int, [_vp, _vp] + [C.c_int] * 7 + [C.c_float, C.c_float, _vp]),
     "vdt_dvs_fc1_recurrent": (C.c_int, [_vp] * 5 + [C.c_int] * 5 + [C.c_float, C.c_float, _vp, _vp]),
     "vdt_dvs_fc2": (C.c_int, [_vp] * 4 + [C.c_int] * 5 + [C.c_float, C.c_float, _vp, _vp]),

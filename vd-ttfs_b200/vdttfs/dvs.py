@@ -86,6 +86,32 @@ def conv_bucketed(buckets, w_hwio, N, C_in, C_out, H, W, spec, out_layout=LAYOUT
     return out
 
 
+def dense_supported(C_in, k):
+    """vdt_dvs_conv_dense handles the layer (K*K*C_in <= 1152, K*K <= 32)."""
+    return k * k <= 32 and k * k * C_in <= 1152
+
+
+def conv_dense(x, w_hwio, N, C_in, C_out, H, W, spec, in_layout=LAYOUT_NCHW, out_layout=LAYOUT_NCHW,
+               stream=None):
+    """k_bucketize_conv + conv_bucketed_early in one launch, straight from the
+    input spike map x (same results as bucketize_sites + conv_bucketed)."""
+    import torch
+    out = torch.empty((N * C_out * H * W,), dtype=torch.float32, device=x.device)
+    check(lib().vdt_dvs_conv_dense(_ptr(x), in_layout, _ptr(w_hwio), N, C_in, C_out, H, W, spec.k, spec.T,
+                                   spec.delta, spec.decay_conv, spec.th_conv, out_layout, _ptr(out),
+                                   C.c_void_p(_stream(stream))), "vdt_dvs_conv_dense")
+    return out
+
+
+def conv_layer(x, w_hwio, N, C_in, C_out, H, W, spec, stream=None):
+    """A bucketed CuLIF conv layer on an NCHW map: the fused kernel where it
+    applies, else bucketize_sites + conv_bucketed."""
+    if dense_supported(C_in, spec.k):
+        return conv_dense(x, w_hwio, N, C_in, C_out, H, W, spec, stream=stream)
+    return conv_bucketed(bucketize_sites(x, N, C_in, H, W, spec, stream), w_hwio, N, C_in, C_out, H, W, spec,
+                         stream=stream)
+
+
 def pool(x, N, Cc, H, W, spec, layout=LAYOUT_NCHW, stream=None):
     import torch
     out = torch.empty((N * Cc * (H // 2) * (W // 2),), dtype=torch.float32, device=x.device)
@@ -136,14 +162,12 @@ def run(spec: nets.DvsSpec, w: DvsWeights, frames, keep=False, stream=None):
     maps = []
     x = conv1_raw(frames, w.conv1, spec0, stream)             # frame windows of the configured width
     maps.append(x)
-    x = conv_bucketed(bucketize_sites(x, N, c1n, H, W, spec, stream), w.conv2, N, c1n, c2n, H, W, spec,
-                      stream=stream)
+    x = conv_layer(x, w.conv2, N, c1n, c2n, H, W, spec, stream)
     maps.append(x)
     x = pool(x, N, c2n, H, W, spec, stream=stream)
     maps.append(x)
     H2, W2 = H // 2, W // 2
-    x = conv_bucketed(bucketize_sites(x, N, c2n, H2, W2, spec, stream), w.conv3, N, c2n, c3n, H2, W2, spec,
-                      stream=stream)
+    x = conv_layer(x, w.conv3, N, c2n, c3n, H2, W2, spec, stream)
     maps.append(x)
     x = pool(x, N, c3n, H2, W2, spec, stream=stream)
     maps.append(x)
