@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(C1_WARPS * 32) k_culif_conv1(const float* __re
                                                                int C_out, int H, int W, int K, int T,
                                                                int NC, float decay, float th) {
     extern __shared__ float c1_sm[];
+    __shared__ long long s_toff[32];                          // per tap: frame offset from the pixel's own
+    __shared__ int s_tdy[32], s_tdx[32];                      // per tap: row / column offset
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int taps = C_in * K * K;                            // <= 32
     float* s_w = c1_sm;                                       // [taps][C_out]
@@ -42,13 +44,18 @@ __global__ void __launch_bounds__(C1_WARPS * 32) k_culif_conv1(const float* __re
         const int q = i / C_out, co = i - q * C_out;
         s_w[i] = __ldg(w_oihw + (long long)co * taps + q);
     }
+    if (threadIdx.x < taps) {                                 // tap q = (c_in, ky, kx), the reference's order
+        const int q = threadIdx.x, ci = q / (K * K), r = q - ci * K * K, ky = r / K, kx = r - ky * K;
+        s_tdy[q] = ky - K / 2;
+        s_tdx[q] = kx - K / 2;
+        s_toff[q] = (((long long)ci * H + (ky - K / 2)) * W + (kx - K / 2)) * T;
+    }
     __syncthreads();
     const long long gw = (long long)blockIdx.x * C1_WARPS + warp;
     if (gw >= (long long)N * H * W) return;
     const int x = (int)(gw % W);
     const int y = (int)((gw / W) % H);
     const long long n = gw / ((long long)W * H);
-    const int pad = K / 2;
     const int c0 = lane * V;
     const bool lane_ok = c0 < C_out;
     const float* wl = s_w + (lane_ok ? c0 : 0);
@@ -56,15 +63,15 @@ __global__ void __launch_bounds__(C1_WARPS * 32) k_culif_conv1(const float* __re
     CulifLanes<V> nu;
     nu.init(lane_ok, 9999.0f);
     const CulifCfg cc{decay, th};
+    // the pixel's own frame row: frames[n][0][y][x][0]
+    const float* fpix = frames + ((n * C_in * H + y) * (long long)W + x) * T;
     for (int tau = 0; tau < NC; ++tau) {
         const int base = tau * DELTA;
         for (int i = lane; i < taps * DELTA; i += 32) {
-            const int q = i / DELTA, t = i - q * DELTA;
-            const int ci = q / (K * K), r = q - ci * K * K, ky = r / K, kx = r - ky * K;
-            const int iy = y + ky - pad, ix = x + kx - pad;
+            const int q = i / DELTA, t = i - q * DELTA;      // DELTA is a power of two
             float v = 0.0f;
-            if (iy >= 0 && iy < H && ix >= 0 && ix < W && base + t < T)
-                v = __ldg(frames + ((((n * C_in + ci) * H + iy) * (long long)W + ix) * T) + base + t);
+            if ((unsigned)(y + s_tdy[q]) < (unsigned)H && (unsigned)(x + s_tdx[q]) < (unsigned)W && base + t < T)
+                v = __ldg(fpix + s_toff[q] + base + t);
             s_f[i] = v;
         }
         __syncwarp();
