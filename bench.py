@@ -9,8 +9,11 @@ int32 predictions when N > 1.
   value   images/s over all ranks, input pixels already in HBM, device-timed
           with CUDA events per step (max over ranks); a 256 MiB L2-flush write
           runs between steps, outside the timed events.
-  e2e     the same through vdt_infer_host: pinned host pixels -> H2D -> the
-          network -> D2H of the logits and predictions, every step.
+  e2e     the same through the host entry points: pinned host pixels -> H2D
+          -> the network -> D2H of the logits and predictions, every step
+          (vdt_infer_host step by step with the L2 flush between steps; for a
+          batch larger than L2, vdt_infer_host_batches, which overlaps step
+          i+1's H2D copy with step i's compute).
   roofline  the bucketize + integrator launches of a step (k_bucketize,
           k_dense, k_sorted, k_integrate, k_layer_vmem), timed live with CUDA
           events around each launch (eager profiling pass), against their
@@ -35,6 +38,8 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "vd-ttfs_b200"))
+
+L2_BYTES = 126 * 1000 * 1000   # B200 L2: a batch larger than this evicts the previous step's data by itself
 
 CONFIGS = {
     # name: (net factory, config id, batch per GPU, zero fraction, scaling)
@@ -236,26 +241,47 @@ def run_engine(a):
         tot_ms = float(t.item())
     value = world * B * a.steps / (tot_ms / 1e3)
 
-    # ---- end to end through host buffers (pinned), every step
+    # ---- end to end through host buffers (pinned), every step.  A batch
+    # larger than L2 goes through the pipelined serving call
+    # (vdt_infer_host_batches: step i+1's H2D copy overlaps step i's compute,
+    # every step's copies inside the timed region); a smaller one step by
+    # step with the L2 flush between steps (vdt_infer_host).
     h_in = torch.from_numpy(img).pin_memory()
-    h_out = torch.empty((B, net.n_classes), dtype=torch.float32).pin_memory()
-    h_pred = torch.empty((B,), dtype=torch.int32).pin_memory()
-    for _ in range(max(1, a.warmup)):
-        ctx.infer_host(h_in, pixels=True, out=h_out, pred=h_pred)
-    if world > 1:
-        dist.barrier()
-    e_times = []
-    for _ in range(a.steps):
+    pipelined = img.nbytes > L2_BYTES
+    if pipelined:
+        h_outs = [torch.empty((B, net.n_classes), dtype=torch.float32).pin_memory() for _ in range(a.steps)]
+        h_preds = [torch.empty((B,), dtype=torch.int32).pin_memory() for _ in range(a.steps)]
+        ctx.infer_host_batches([h_in] * 2, pixels=True, outs=h_outs[:2], preds=h_preds[:2])   # both slots' graphs
+        if world > 1:
+            dist.barrier()
         with torch.cuda.stream(stream):
-            flush.fill_(1)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-        ctx.infer_host(h_in, pixels=True, out=h_out, pred=h_pred)
+        ctx.infer_host_batches([h_in] * a.steps, pixels=True, outs=h_outs, preds=h_preds)
         with torch.cuda.stream(stream):
             e1.record(stream)
         stream.synchronize()
-        e_times.append(e0.elapsed_time(e1))
+        e_times = [e0.elapsed_time(e1)]
+    else:
+        h_out = torch.empty((B, net.n_classes), dtype=torch.float32).pin_memory()
+        h_pred = torch.empty((B,), dtype=torch.int32).pin_memory()
+        for _ in range(max(1, a.warmup)):
+            ctx.infer_host(h_in, pixels=True, out=h_out, pred=h_pred)
+        if world > 1:
+            dist.barrier()
+        e_times = []
+        for _ in range(a.steps):
+            with torch.cuda.stream(stream):
+                flush.fill_(1)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            ctx.infer_host(h_in, pixels=True, out=h_out, pred=h_pred)
+            with torch.cuda.stream(stream):
+                e1.record(stream)
+            stream.synchronize()
+            e_times.append(e0.elapsed_time(e1))
     e_ms = float(np.sum(e_times))
     if world > 1:
         t = torch.tensor([e_ms], device=dev)
@@ -297,7 +323,9 @@ def run_engine(a):
                        "zero_frac": zf, "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) between steps"},
             "e2e": {"value": round(e2e, 1), "unit": "images/s",
                     "h2d_bytes_per_step": int(img.nbytes),
-                    "d2h_bytes_per_step": int(B * net.n_classes * 4 + B * 4)},
+                    "d2h_bytes_per_step": int(B * net.n_classes * 4 + B * 4),
+                    "api": "vdt_infer_host_batches (pipelined, batch > L2)" if pipelined
+                    else "vdt_infer_host per step, L2 flushed between steps"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic_per_step(netname, B),
@@ -529,8 +557,14 @@ def run_dvs_engine(a):
         dist.barrier()
     clocks = ClockSampler(local, enabled=(rank == 0 and not a.no_clocks))
     clocks.start()
+    # frames larger than L2 evict the previous step by themselves; smaller
+    # ones get the 256 MiB flush write between steps, outside the events
+    big = frames.nbytes > L2_BYTES
+    flush = None if big else torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     times = []
     for _ in range(a.steps):
+        if flush is not None:
+            flush.fill_(1)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         step(x_dev)
@@ -545,22 +579,31 @@ def run_dvs_engine(a):
         tot_ms = float(t.item())
     value = world * B * a.steps / (tot_ms / 1e3)
 
-    # end to end: pinned host frames -> device, the network, outputs back
+    # end to end: pinned host frames -> device, the network, outputs back,
+    # every step.  Frames larger than L2 go through dvs.run_host_batches
+    # (step i+1's frames cross while step i computes); smaller ones step by
+    # step through the same call with one batch, the L2 flush between steps.
     h_in = torch.from_numpy(frames).pin_memory()
-    h_out = torch.empty((B, spec.classes), dtype=torch.float32).pin_memory()
-    h_pred = torch.empty((B,), dtype=torch.int32).pin_memory()
-    x_e2e = torch.empty_like(x_dev)
-    e_times = []
-    for it in range(a.steps + 1):
+    h_outs = [torch.empty((B, spec.classes), dtype=torch.float32).pin_memory() for _ in range(a.steps)]
+    h_preds = [torch.empty((B,), dtype=torch.int32).pin_memory() for _ in range(a.steps)]
+    dvs.run_host_batches(spec, w, [h_in] * 2, h_outs[:2], h_preds[:2])   # warms the copies
+    torch.cuda.synchronize()
+    if big:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        x_e2e.copy_(h_in, non_blocking=True)
-        y, pred, _ = dvs_stages(dvs, spec, w, x_e2e, B)
-        h_out.copy_(y.reshape(B, spec.classes), non_blocking=True)
-        h_pred.copy_(pred, non_blocking=True)
+        dvs.run_host_batches(spec, w, [h_in] * a.steps, h_outs, h_preds)
         e1.record(stream)
         torch.cuda.synchronize()
-        if it > 0:                                           # the first pass warms the copies
+        e_times = [e0.elapsed_time(e1)]
+    else:
+        e_times = []
+        for i in range(a.steps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            dvs.run_host_batches(spec, w, [h_in], h_outs[i:i + 1], h_preds[i:i + 1])
+            e1.record(stream)
+            torch.cuda.synchronize()
             e_times.append(e0.elapsed_time(e1))
     e_ms = float(np.sum(e_times))
     if world > 1:
@@ -592,9 +635,13 @@ def run_dvs_engine(a):
             "config": {"workload": f"{netname} C{cfg_id}",
                        "model": f"dvs-culif {spec.in_c}x{spec.H}x{spec.W}, {spec.classes} classes",
                        "global_batch": world * B, "batch_per_gpu": B, "T": spec.T, "delta": spec.delta,
-                       "parallelism": f"dp{world}", "l2": "inputs larger than L2 (frames 21 MB per sample)"},
+                       "parallelism": f"dp{world}",
+                       "l2": (f"inputs larger than L2 (frames {frames.nbytes / B / 1e6:.1f} MB per sample)" if big
+                              else "flushed (256 MiB write) between steps")},
             "e2e": {"value": round(e2e, 1), "unit": "samples/s", "h2d_bytes_per_step": int(frames.nbytes),
-                    "d2h_bytes_per_step": int(B * spec.classes * 4 + B * 4)},
+                    "d2h_bytes_per_step": int(B * spec.classes * 4 + B * 4),
+                    "api": "dvs.run_host_batches (pipelined, frames > L2)" if big
+                    else "dvs.run_host_batches one batch per step, L2 flushed between steps"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": None,
                          "kernel": "all DVS stages of one step", "peak_source": f"{peak_kind} hbm_gbs",

@@ -174,6 +174,16 @@ int vdt_infer(vdt_ctx* c, const float* d_input, int input_is_pixels, int batch,
    D2H copy of outputs; synchronous. */
 int vdt_infer_host(vdt_ctx* c, const float* h_input, int input_is_pixels, int batch,
                    float* h_out, int32_t* h_pred);
+/* n_batches batches of `batch` images each, end to end from host buffers,
+   pipelined: batch i+1's H2D copy (a second input slot, a copy stream) runs
+   while batch i computes, and batch i's D2H copy while batch i+1 computes.
+   h_inputs[i] (pinned host memory for the overlap to happen) must stay valid
+   until the call returns; h_outs / h_preds (or any entry of them) may be
+   NULL.  Same results as n_batches calls of vdt_infer_host; synchronous.
+   The serving loop around the reference's per-batch body (t1:290-315,
+   t2:341-392), which copies, computes and copies back in turn. */
+int vdt_infer_host_batches(vdt_ctx* c, int n_batches, const float* const* h_inputs, int input_is_pixels,
+                           int batch, float* const* h_outs, int32_t* const* h_preds);
 /* Same as vdt_infer, also writing every layer's output map (before its pool)
    into d_layer_out[i] (device buffers sized [batch, H_out, W_out, C_out]). */
 int vdt_infer_trace(vdt_ctx* c, const float* d_input, int input_is_pixels, int batch,

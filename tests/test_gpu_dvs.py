@@ -111,6 +111,21 @@ def test_conv_dense_rejects_large_fan_in(dev):
     assert ei.value.status == 5
 
 
+def test_run_host_batches_pipelined(dev):
+    """dvs.run_host_batches (next batch's frames copied while this batch
+    runs) gives each batch run()'s outputs and predictions."""
+    import torch
+    from vdttfs import dvs, nets, synth
+    spec = nets.dvs_ref()
+    w = dvs.DvsWeights(spec, synth.dvs_weights(spec, 4), dev)
+    frames = [torch.from_numpy(synth.dvs_frames(4, 3, spec, stream=40 + i)).pin_memory() for i in range(3)]
+    refs = [dvs.run(spec, w, f.to(dev)) for f in frames]
+    outs, preds = dvs.run_host_batches(spec, w, frames)
+    for i in range(3):
+        assert bits_equal(outs[i].numpy(), _np(refs[i]["out"])), f"batch {i}"
+        assert np.array_equal(preds[i].numpy(), _np(refs[i]["pred"]))
+
+
 @pytest.mark.parametrize("layout", [0, 1])
 def test_pool_chunk_early(O, dev, layout):
     from vdttfs import dvs, nets

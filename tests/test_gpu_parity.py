@@ -362,6 +362,37 @@ def test_infer_host_matches_device_and_eager(O, dev):
     assert bits_equal(o4, o2[:3])
 
 
+@pytest.mark.parametrize("graphs", [True, False])
+def test_infer_host_batches_pipelined(O, dev, graphs):
+    """vdt_infer_host_batches (next batch's H2D overlapping this batch's
+    compute, two device slots) gives every batch the result vdt_infer_host
+    gives it, for 1 to 5 batches of different inputs, graph and eager paths;
+    NULL output entries are skipped and bad arguments are rejected."""
+    import torch
+    from vdttfs import engine as E, synth
+    net, layers, _ = _net_case("lenet5", 4, 1, 0.8)
+    m = E.Model(net, layers)
+    ctx = E.Context(m, 16)
+    ctx.set_graphs(graphs)
+    imgs = [torch.from_numpy(synth.images(1, 16, 28, 28, 1, 0.8, stream=30 + i)).pin_memory() for i in range(5)]
+    refs = [ctx.infer_host(x.numpy(), pixels=True) for x in imgs]
+    for n in (1, 2, 5):
+        outs, preds = ctx.infer_host_batches(imgs[:n], pixels=True)
+        for i in range(n):
+            assert bits_equal(outs[i], refs[i][0]), f"n={n} batch {i}"
+            assert np.array_equal(preds[i], refs[i][1])
+    assert ctx.infer_host_batches([], pixels=True) == ([], [])
+    import ctypes as C
+    from vdttfs._lib import lib
+    arr = (C.c_void_p * 2)(imgs[0].data_ptr(), None)
+    outs = (C.c_void_p * 2)(None, None)
+    assert lib().vdt_infer_host_batches(ctx.h, 2, arr, 1, 16, outs, outs) == 1      # h_inputs[1] NULL
+    assert lib().vdt_infer_host_batches(ctx.h, 1, arr, 1, 17, None, None) == 6      # batch > max_batch (VDT_ERR_CAPACITY)
+    assert lib().vdt_infer_host_batches(ctx.h, 1, arr, 1, 16, None, None) == 0      # no outputs wanted
+    ctx.close()
+    m.close()
+
+
 def test_launch_overlap_changes_nothing(O, dev):
     """Programmatic dependent launch on and off: identical maps and outputs,
     through the captured graph and the eager path."""

@@ -173,9 +173,9 @@ struct vdt_model {
 };
 
 struct GraphKey {
-    int batch, pixels, counting;
+    int batch, pixels, counting, slot;
     bool operator<(const GraphKey& o) const {
-        return std::tie(batch, pixels, counting) < std::tie(o.batch, o.pixels, o.counting);
+        return std::tie(batch, pixels, counting, slot) < std::tie(o.batch, o.pixels, o.counting, o.slot);
     }
 };
 
@@ -188,6 +188,13 @@ struct vdt_ctx {
     float* in_slot = nullptr;    // [max_batch, in_h, in_w, in_c]
     float* out_slot = nullptr;   // [max_batch, classes]
     int32_t* pred_slot = nullptr;
+    // second input/output slot, copy stream and events of the pipelined host
+    // path (vdt_infer_host_batches), made on its first call
+    float* in_slot2 = nullptr;
+    float* out_slot2 = nullptr;
+    int32_t* pred_slot2 = nullptr;
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t ev_h2d[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
     int* off = nullptr;
     int* cin = nullptr;
     float* tin = nullptr;
@@ -481,6 +488,12 @@ void ctx_free(vdt_ctx* c) {
     c->cache.clear();
     for (auto& a : c->act) cudaFree(a);
     cudaFree(c->in_slot); cudaFree(c->out_slot); cudaFree(c->pred_slot);
+    cudaFree(c->in_slot2); cudaFree(c->out_slot2); cudaFree(c->pred_slot2);
+    for (int i = 0; i < 2; ++i) {
+        if (c->ev_h2d[i]) cudaEventDestroy(c->ev_h2d[i]);
+        if (c->ev_done[i]) cudaEventDestroy(c->ev_done[i]);
+    }
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     cudaFree(c->off); cudaFree(c->cin); cudaFree(c->tin); cudaFree(c->counters);
 }
 
@@ -715,11 +728,14 @@ extern "C" int vdt_ctx_set_layer_kernel(vdt_ctx* c, int layer, int kernel) {
     return VDT_OK;
 }
 
-// Run one batch from ctx->in_slot into ctx->out_slot / pred_slot, through a
-// cached CUDA graph when enabled.
-static int run_slots(vdt_ctx* c, int pixels, int batch) {
-    if (!c->graphs || c->profiling) return enqueue(c, c->in_slot, pixels, batch, c->out_slot, c->pred_slot, nullptr);
-    const GraphKey key{batch, pixels, c->counting ? 1 : 0};
+// Run one batch from the ctx's input slot `slot` (0: in_slot, 1: in_slot2)
+// into the matching output slots, through a cached CUDA graph when enabled.
+static int run_slots(vdt_ctx* c, int pixels, int batch, int slot = 0) {
+    float* in = slot ? c->in_slot2 : c->in_slot;
+    float* out = slot ? c->out_slot2 : c->out_slot;
+    int32_t* pred = slot ? c->pred_slot2 : c->pred_slot;
+    if (!c->graphs || c->profiling) return enqueue(c, in, pixels, batch, out, pred, nullptr);
+    const GraphKey key{batch, pixels, c->counting ? 1 : 0, slot};
     auto it = c->cache.find(key);
     if (it == c->cache.end()) {
         // capture on a private stream: the legacy default stream can't be captured
@@ -730,7 +746,7 @@ static int run_slots(vdt_ctx* c, int pixels, int batch) {
         cudaGraph_t graph = nullptr;
         cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
         int st = VDT_OK;
-        if (e == cudaSuccess) st = enqueue(c, c->in_slot, pixels, batch, c->out_slot, c->pred_slot, nullptr);
+        if (e == cudaSuccess) st = enqueue(c, in, pixels, batch, out, pred, nullptr);
         cudaError_t e2 = cudaStreamEndCapture(cap, &graph);
         c->stream = user;
         cudaStreamDestroy(cap);
@@ -794,6 +810,70 @@ extern "C" int vdt_infer_host(vdt_ctx* c, const float* h_input, int input_is_pix
     if (h_pred)
         VDT_CUDA(cudaMemcpyAsync(h_pred, c->pred_slot, (size_t)batch * sizeof(int32_t),
                                  cudaMemcpyDeviceToHost, c->stream));
+    VDT_CUDA(cudaStreamSynchronize(c->stream));
+    return VDT_OK;
+}
+
+// Resources of the pipelined host path, made once per ctx.
+static int ensure_pipeline(vdt_ctx* c) {
+    if (c->copy_stream) return VDT_OK;
+    const vdt_model* m = c->m;
+    const size_t in_n = (size_t)c->max_batch * m->net.in_h * m->net.in_w * m->net.in_c;
+    cudaError_t e = cudaMalloc(&c->in_slot2, in_n * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->out_slot2, (size_t)c->max_batch * m->n_classes * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&c->pred_slot2, (size_t)c->max_batch * sizeof(int32_t));
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
+        e = cudaEventCreateWithFlags(&c->ev_h2d[i], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_done[i], cudaEventDisableTiming);
+    }
+    cudaStream_t cs = nullptr;
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cuda_fail(e, "pipelined host path resources");
+    c->copy_stream = cs;
+    return VDT_OK;
+}
+
+extern "C" int vdt_infer_host_batches(vdt_ctx* c, int n_batches, const float* const* h_inputs,
+                                      int input_is_pixels, int batch, float* const* h_outs,
+                                      int32_t* const* h_preds) {
+    g_last_error.clear();
+    if (int s = check_batch(c, batch)) return s;
+    if (n_batches < 0 || (n_batches > 0 && !h_inputs)) return fail(VDT_ERR_INVALID, "n_batches / h_inputs");
+    for (int i = 0; i < n_batches; ++i)
+        if (!h_inputs[i]) return fail(VDT_ERR_INVALID, "h_inputs[%d] is NULL", i);
+    if (n_batches == 0) return VDT_OK;
+    DeviceGuard g(c->m->device);
+    if (int s = ensure_pipeline(c)) return s;
+    const vdt_model* m = c->m;
+    const size_t in_bytes = (size_t)batch * m->net.in_h * m->net.in_w * m->net.in_c * sizeof(float);
+    const size_t out_bytes = (size_t)batch * m->n_classes * sizeof(float);
+    const size_t pred_bytes = (size_t)batch * sizeof(int32_t);
+    float* const ins[2] = {c->in_slot, c->in_slot2};
+    float* const outs[2] = {c->out_slot, c->out_slot2};
+    int32_t* const preds[2] = {c->pred_slot, c->pred_slot2};
+    cudaStream_t cs = c->copy_stream;
+    // batch i uses slot i % 2.  Copy stream: H2D(0), H2D(1), then per batch
+    // i: D2H(i) after its compute, H2D(i + 2) once compute(i) has released
+    // the slot.  The ctx stream runs compute(i) once H2D(i) has landed.
+    VDT_CUDA(cudaMemcpyAsync(ins[0], h_inputs[0], in_bytes, cudaMemcpyHostToDevice, cs));
+    VDT_CUDA(cudaEventRecord(c->ev_h2d[0], cs));
+    for (int i = 0; i < n_batches; ++i) {
+        const int s = i & 1;
+        VDT_CUDA(cudaStreamWaitEvent(c->stream, c->ev_h2d[s], 0));
+        if (int st = run_slots(c, input_is_pixels, batch, s)) return st;
+        VDT_CUDA(cudaEventRecord(c->ev_done[s], c->stream));
+        if (i + 1 < n_batches) {                             // next input, overlapping compute(i)
+            const int s1 = (i + 1) & 1;
+            if (i >= 1) VDT_CUDA(cudaStreamWaitEvent(cs, c->ev_done[s1], 0));   // compute(i - 1) left the slot
+            VDT_CUDA(cudaMemcpyAsync(ins[s1], h_inputs[i + 1], in_bytes, cudaMemcpyHostToDevice, cs));
+            VDT_CUDA(cudaEventRecord(c->ev_h2d[s1], cs));
+        }
+        VDT_CUDA(cudaStreamWaitEvent(cs, c->ev_done[s], 0));
+        if (h_outs && h_outs[i]) VDT_CUDA(cudaMemcpyAsync(h_outs[i], outs[s], out_bytes, cudaMemcpyDeviceToHost, cs));
+        if (h_preds && h_preds[i])
+            VDT_CUDA(cudaMemcpyAsync(h_preds[i], preds[s], pred_bytes, cudaMemcpyDeviceToHost, cs));
+    }
+    VDT_CUDA(cudaStreamSynchronize(cs));
     VDT_CUDA(cudaStreamSynchronize(c->stream));
     return VDT_OK;
 }

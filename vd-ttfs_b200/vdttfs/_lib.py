@@ -58,6 +58,7 @@ SIGNATURES = {
     "vdt_ctx_layer_times": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _ip]),
     "vdt_infer": (C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp, _vp]),
     "vdt_infer_host": (C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp, _vp]),
+    "vdt_infer_host_batches": (C.c_int, [_vp, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]),
     "vdt_infer_trace": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.POINTER(C.c_void_p), _vp, _vp]),
     "vdt_build_luts": (C.c_int, [C.c_int, C.c_int, C.c_float, C.c_float, C.c_float, C.c_float,
                                  C.c_float, _vp, _vp, _vp]),

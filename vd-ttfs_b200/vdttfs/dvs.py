@@ -181,3 +181,52 @@ def run(spec: nets.DvsSpec, w: DvsWeights, frames, keep=False, stream=None):
     if keep:
         res["maps"] = maps
     return res
+
+
+def run_host_batches(spec: nets.DvsSpec, w: DvsWeights, h_frames, outs=None, preds=None):
+    """Several batches end to end from host memory, pipelined: batch i+1's
+    frames are copied (a second device slot, a copy stream) while batch i
+    runs on the current stream, and batch i's outputs are copied back while
+    batch i+1 runs.  h_frames: pinned CPU tensors [N, C_in, H, W, T] of one
+    shape; outs / preds: per batch, pinned tensors [N, classes] / [N]
+    (allocated when None).  Same results as run() per batch; synchronous."""
+    import torch
+    n = len(h_frames)
+    if n == 0:
+        return [], []
+    dev = w.conv1.device
+    N = h_frames[0].shape[0]
+    if outs is None:
+        outs = [torch.empty((N, spec.classes), dtype=torch.float32).pin_memory() for _ in range(n)]
+    if preds is None:
+        preds = [torch.empty((N,), dtype=torch.int32).pin_memory() for _ in range(n)]
+    comp = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)
+    slots = [torch.empty(h_frames[0].shape, dtype=torch.float32, device=dev) for _ in range(min(2, n))]
+    h2d = [torch.cuda.Event(), torch.cuda.Event()]
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+    with torch.cuda.stream(copy):
+        slots[0].copy_(h_frames[0], non_blocking=True)
+        h2d[0].record(copy)
+    for i in range(n):
+        s = i & 1
+        comp.wait_event(h2d[s])
+        r = run(spec, w, slots[s])
+        done[s].record(comp)
+        if i + 1 < n:                                         # next frames, overlapping this batch
+            s1 = (i + 1) & 1
+            with torch.cuda.stream(copy):
+                if i >= 1:
+                    copy.wait_event(done[s1])                 # batch i - 1 left the slot
+                slots[s1].copy_(h_frames[i + 1], non_blocking=True)
+                h2d[s1].record(copy)
+        with torch.cuda.stream(copy):
+            copy.wait_event(done[s])
+            outs[i].copy_(r["out"], non_blocking=True)
+            preds[i].copy_(r["pred"], non_blocking=True)
+        r["out"].record_stream(copy)                          # not reused before its copy ends
+        r["pred"].record_stream(copy)
+    copy.synchronize()
+    comp.synchronize()
+    return outs, preds
+

@@ -180,6 +180,29 @@ class Context:
         check(lib().vdt_infer_host(self.h, hp(x), int(pixels), B, hp(out), hp(pred)), "vdt_infer_host")
         return out, pred
 
+    def infer_host_batches(self, xs, pixels: bool = False, outs=None, preds=None):
+        """Several batches end to end from host memory, pipelined
+        (vdt_infer_host_batches: the next batch's H2D copy overlaps this
+        batch's compute).  xs: host arrays / pinned CPU tensors, all of one
+        batch size; outs / preds: per batch, allocated when None."""
+        n = len(xs)
+        if n == 0:
+            return [], []
+        B = xs[0].shape[0]
+        if any(x.shape[0] != B for x in xs):
+            raise ValueError("every batch must have the same size")
+        if outs is None:
+            outs = [np.empty((B, self.model.n_classes), np.float32) for _ in range(n)]
+        if preds is None:
+            preds = [np.empty((B,), np.int32) for _ in range(n)]
+
+        def hp(a):
+            return a.ctypes.data if isinstance(a, np.ndarray) else a.data_ptr()
+        arr = lambda items: (C.c_void_p * n)(*[hp(a) for a in items])
+        check(lib().vdt_infer_host_batches(self.h, n, arr(xs), int(pixels), B, arr(outs), arr(preds)),
+              "vdt_infer_host_batches")
+        return outs, preds
+
     def trace(self, x, pixels: bool = False):
         """Whole network, returning every layer's output map (before pooling)."""
         import torch
