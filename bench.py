@@ -192,6 +192,7 @@ def run_engine(a):
     model = E.Model(net, layers, device=local)
     stream = torch.cuda.Stream(device=dev)
     ctx = E.Context(model, B, stream=stream.cuda_stream)
+    ctx.set_sub_batches(2)      # two halves of the batch on two streams (same results)
 
     x_dev = torch.from_numpy(img).to(dev)
     out = torch.empty((B, net.n_classes), dtype=torch.float32, device=dev)
@@ -320,7 +321,8 @@ def run_engine(a):
             "data": "synthetic (seeded uniform pixels, Kaiming weights, see vdttfs/synth.py)",
             "config": {"workload": f"{netname} C{cfg_id}", "model": netname, "global_batch": world * B,
                        "batch_per_gpu": B, "T": net.T, "delta": net.delta, "fire_start": net.tfs,
-                       "zero_frac": zf, "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) between steps"},
+                       "zero_frac": zf, "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) between steps",
+                       "sub_batches": 2},
             "e2e": {"value": round(e2e, 1), "unit": "images/s",
                     "h2d_bytes_per_step": int(img.nbytes),
                     "d2h_bytes_per_step": int(B * net.n_classes * 4 + B * 4),

@@ -393,6 +393,35 @@ def test_infer_host_batches_pipelined(O, dev, graphs):
     m.close()
 
 
+@pytest.mark.parametrize("name,B", [("vgg16", 5), ("lenet5", 33), ("vgg16", 1)])
+def test_sub_batches_change_nothing(O, dev, name, B):
+    """vdt_ctx_set_sub_batches(2) (two halves of each batch on two streams,
+    graph and eager paths, device and pipelined host entry points) gives the
+    whole batch's outputs and predictions bit for bit, odd batches included."""
+    from vdttfs import engine as E
+    net, layers, img = _net_case(name, B, 3 if name == "vgg16" else 1, 0.0 if name == "vgg16" else 0.8)
+    spikes = O.encode_linear(img, net.T)
+    ref = O.run_net(net, layers, spikes)
+    m = E.Model(net, layers, lut_source=E.LUT_HOST_LIBM)
+    ctx = E.Context(m, B)
+    ctx.set_sub_batches(2)
+    for graphs in (True, False):
+        ctx.set_graphs(graphs)
+        out, pred = ctx.infer(_t(spikes, dev))
+        _sync()
+        assert bits_equal(_np(out), ref["out"]) and np.array_equal(_np(pred), ref["pred"]), f"graphs={graphs}"
+    outs, preds = ctx.infer_host_batches([spikes, spikes])
+    assert all(bits_equal(o, ref["out"]) for o in outs) and all(np.array_equal(p, ref["pred"]) for p in preds)
+    ctx.set_counting(True)                                   # counting passes run whole batches
+    out, _ = ctx.infer(_t(spikes, dev))
+    _sync()
+    assert bits_equal(_np(out), ref["out"])
+    with pytest.raises(E.VdtError):
+        ctx.set_sub_batches(3)
+    ctx.close()
+    m.close()
+
+
 def test_launch_overlap_changes_nothing(O, dev):
     """Programmatic dependent launch on and off: identical maps and outputs,
     through the captured graph and the eager path."""

@@ -195,6 +195,15 @@ struct vdt_ctx {
     int32_t* pred_slot2 = nullptr;
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_h2d[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
+    // sub-batches (vdt_ctx_set_sub_batches): the second half of a batch runs
+    // on sub_stream with its own activation and bucket workspace
+    int n_sub = 1;
+    float* act2[3] = {nullptr, nullptr, nullptr};
+    int* off2 = nullptr;
+    int* cin2 = nullptr;
+    float* tin2 = nullptr;
+    cudaStream_t sub_stream = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     int* off = nullptr;
     int* cin = nullptr;
     float* tin = nullptr;
@@ -494,6 +503,11 @@ void ctx_free(vdt_ctx* c) {
         if (c->ev_done[i]) cudaEventDestroy(c->ev_done[i]);
     }
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+    for (auto& a : c->act2) cudaFree(a);
+    cudaFree(c->off2); cudaFree(c->cin2); cudaFree(c->tin2);
+    if (c->ev_fork) cudaEventDestroy(c->ev_fork);
+    if (c->ev_join) cudaEventDestroy(c->ev_join);
+    if (c->sub_stream) cudaStreamDestroy(c->sub_stream);
     cudaFree(c->off); cudaFree(c->cin); cudaFree(c->tin); cudaFree(c->counters);
 }
 
@@ -594,7 +608,68 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
     return VDT_OK;
 }
 
+// One batch, split in two halves on two streams when sub-batches are on (the
+// first half on the ctx stream, the second on sub_stream with the second
+// workspace; each half is an independent run of the same per-batch body, so
+// the results are those of one run).  Counting and profiling passes run
+// whole.
+int enqueue_split(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, int32_t* d_pred) {
+    if (c->n_sub < 2 || B < 2 || c->counting || c->profiling)
+        return enqueue(c, d_input, pixels, B, d_out, d_pred, nullptr);
+    const vdt_model* m = c->m;
+    const int b1 = (B + 1) / 2, b2 = B - b1;
+    const size_t in_row = (size_t)m->net.in_h * m->net.in_w * m->net.in_c;
+    cudaStream_t s = c->stream;
+    VDT_CUDA(cudaEventRecord(c->ev_fork, s));
+    VDT_CUDA(cudaStreamWaitEvent(c->sub_stream, c->ev_fork, 0));
+    if (int st = enqueue(c, d_input, pixels, b1, d_out, d_pred, nullptr)) return st;
+    // the second half: the ctx's stream and workspace swapped for the second set
+    auto swap_ws = [c] {
+        std::swap(c->stream, c->sub_stream);
+        for (int i = 0; i < 3; ++i) std::swap(c->act[i], c->act2[i]);
+        std::swap(c->off, c->off2);
+        std::swap(c->cin, c->cin2);
+        std::swap(c->tin, c->tin2);
+    };
+    swap_ws();
+    const int st = enqueue(c, d_input + (size_t)b1 * in_row, pixels, b2, d_out + (size_t)b1 * m->n_classes,
+                           d_pred ? d_pred + b1 : nullptr, nullptr);
+    swap_ws();
+    if (st) return st;
+    VDT_CUDA(cudaEventRecord(c->ev_join, c->sub_stream));
+    VDT_CUDA(cudaStreamWaitEvent(s, c->ev_join, 0));
+    return VDT_OK;
+}
+
 }  // namespace
+
+extern "C" int vdt_ctx_set_sub_batches(vdt_ctx* c, int n) {
+    g_last_error.clear();
+    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    if (n != 1 && n != 2) return fail(VDT_ERR_INVALID, "n=%d (1 or 2)", n);
+    DeviceGuard g(c->m->device);
+    if (n == 2 && !c->sub_stream) {
+        const Sizes z = ctx_sizes(c->m, (c->max_batch + 1) / 2);
+        cudaError_t e = cudaSuccess;
+        for (auto& a : c->act2) if (e == cudaSuccess) e = cudaMalloc(&a, z.act * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&c->off2, std::max<size_t>(z.off, 1) * sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&c->cin2, std::max<size_t>(z.bkt, 1) * sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&c->tin2, std::max<size_t>(z.bkt, 1) * sizeof(float));
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming);
+        cudaStream_t ss = nullptr;
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ss, cudaStreamNonBlocking);
+        if (e != cudaSuccess) return cuda_fail(e, "sub-batch workspace");
+        c->sub_stream = ss;
+    }
+    if (c->n_sub != n) {
+        VDT_CUDA(cudaStreamSynchronize(c->stream));
+        for (auto& kv : c->cache) cudaGraphExecDestroy(kv.second);   // captured with the old split
+        c->cache.clear();
+        c->n_sub = n;
+    }
+    return VDT_OK;
+}
 
 extern "C" int vdt_ctx_create(const vdt_model* m, int max_batch, vdt_stream stream, vdt_ctx** out) {
     g_last_error.clear();
@@ -734,7 +809,7 @@ static int run_slots(vdt_ctx* c, int pixels, int batch, int slot = 0) {
     float* in = slot ? c->in_slot2 : c->in_slot;
     float* out = slot ? c->out_slot2 : c->out_slot;
     int32_t* pred = slot ? c->pred_slot2 : c->pred_slot;
-    if (!c->graphs || c->profiling) return enqueue(c, in, pixels, batch, out, pred, nullptr);
+    if (!c->graphs || c->profiling) return enqueue_split(c, in, pixels, batch, out, pred);
     const GraphKey key{batch, pixels, c->counting ? 1 : 0, slot};
     auto it = c->cache.find(key);
     if (it == c->cache.end()) {
@@ -746,7 +821,7 @@ static int run_slots(vdt_ctx* c, int pixels, int batch, int slot = 0) {
         cudaGraph_t graph = nullptr;
         cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
         int st = VDT_OK;
-        if (e == cudaSuccess) st = enqueue(c, in, pixels, batch, out, pred, nullptr);
+        if (e == cudaSuccess) st = enqueue_split(c, in, pixels, batch, out, pred);
         cudaError_t e2 = cudaStreamEndCapture(cap, &graph);
         c->stream = user;
         cudaStreamDestroy(cap);
@@ -779,7 +854,7 @@ extern "C" int vdt_infer(vdt_ctx* c, const float* d_input, int input_is_pixels, 
     DeviceGuard g(c->m->device);
     const vdt_model* m = c->m;
     const size_t in_n = (size_t)batch * m->net.in_h * m->net.in_w * m->net.in_c;
-    if (!c->graphs || c->profiling) return enqueue(c, d_input, input_is_pixels, batch, d_out, d_pred, nullptr);
+    if (!c->graphs || c->profiling) return enqueue_split(c, d_input, input_is_pixels, batch, d_out, d_pred);
     VDT_CUDA(cudaMemcpyAsync(c->in_slot, d_input, in_n * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
     if (int s = run_slots(c, input_is_pixels, batch)) return s;
     VDT_CUDA(cudaMemcpyAsync(d_out, c->out_slot, (size_t)batch * m->n_classes * sizeof(float),
@@ -802,7 +877,7 @@ extern "C" int vdt_infer_host(vdt_ctx* c, const float* h_input, int input_is_pix
     if (c->graphs) {
         if (int s = run_slots(c, input_is_pixels, batch)) return s;
     } else {
-        if (int s = enqueue(c, c->in_slot, input_is_pixels, batch, c->out_slot, c->pred_slot, nullptr)) return s;
+        if (int s = enqueue_split(c, c->in_slot, input_is_pixels, batch, c->out_slot, c->pred_slot)) return s;
     }
     if (h_out)
         VDT_CUDA(cudaMemcpyAsync(h_out, c->out_slot, (size_t)batch * m->n_classes * sizeof(float),

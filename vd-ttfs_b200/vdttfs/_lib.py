@@ -75,6 +75,7 @@ SIGNATURES = {
     "vdt_readout": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_float, _vp, _vp]),
     "vdt_ctx_layer_kernels": (C.c_int, [_vp, C.c_int, _vp]),
     "vdt_ctx_set_layer_kernel": (C.c_int, [_vp, C.c_int, C.c_int]),
+    "vdt_ctx_set_sub_batches": (C.c_int, [_vp, C.c_int]),
     "vdt_dvs_conv1_raw": (C.c_int, [_vp, _vp] + [C.c_int] * 8 + [C.c_float, C.c_float, _vp, _vp]),
     "vdt_dvs_conv_bucketed": (C.c_int, [_vp, _vp, _vp, _vp] + [C.c_int] * 8 +
                               [C.c_float, C.c_float, C.c_int, _vp, _vp]),

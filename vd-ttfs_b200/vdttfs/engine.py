@@ -122,6 +122,10 @@ class Context:
     def set_graphs(self, on: bool):
         check(lib().vdt_ctx_set_graphs(self.h, int(on)), "vdt_ctx_set_graphs")
 
+    def set_sub_batches(self, n: int):
+        """1 or 2: run each batch as n halves on n streams (same results)."""
+        check(lib().vdt_ctx_set_sub_batches(self.h, int(n)), "vdt_ctx_set_sub_batches")
+
     def set_counting(self, on: bool):
         check(lib().vdt_ctx_set_counting(self.h, int(on)), "vdt_ctx_set_counting")
 
