@@ -160,13 +160,15 @@ int vdt_ctx_layer_kernels(const vdt_ctx* c, int n_layers, int* kernels);
    kernel cannot run the layer.  Drops the ctx's captured graphs. */
 int vdt_ctx_set_layer_kernel(vdt_ctx* c, int layer, int kernel);
 
-/* n = 2: every batch of 2 or more images runs as two halves on two streams
-   (the ctx stream and one of its own, with a second activation / bucket
-   workspace sized for half of max_batch), so one half's small late layers
-   overlap the other half's work; n = 1 (default): one run.  Results are the
-   same either way (each image's computation does not depend on the rest of
-   its batch).  Counting, profiling and vdt_infer_trace run whole batches.
-   Drops the ctx's captured graphs.  No reference counterpart. */
+/* n in [1, VDT_MAX_SUB_BATCHES]: every batch runs as n near-equal parts on n
+   streams (the ctx stream and n - 1 of the ctx's own, each with an
+   activation / bucket workspace sized for max_batch / n, made once and kept),
+   so one part's small late layers overlap the other parts' work; n = 1
+   (default): one run.  Results are the same either way (each image's
+   computation does not depend on the rest of its batch).  Counting,
+   profiling and vdt_infer_trace run whole batches.  Drops the ctx's captured
+   graphs.  No reference counterpart. */
+#define VDT_MAX_SUB_BATCHES 4
 int vdt_ctx_set_sub_batches(vdt_ctx* c, int n);
 
 /* ------------------------------------------------------------------------

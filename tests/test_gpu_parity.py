@@ -395,29 +395,31 @@ def test_infer_host_batches_pipelined(O, dev, graphs):
 
 @pytest.mark.parametrize("name,B", [("vgg16", 5), ("lenet5", 33), ("vgg16", 1)])
 def test_sub_batches_change_nothing(O, dev, name, B):
-    """vdt_ctx_set_sub_batches(2) (two halves of each batch on two streams,
-    graph and eager paths, device and pipelined host entry points) gives the
-    whole batch's outputs and predictions bit for bit, odd batches included."""
+    """vdt_ctx_set_sub_batches(n) (each batch as n parts on n streams, graph
+    and eager paths, device and pipelined host entry points) gives the whole
+    batch's outputs and predictions bit for bit, for n = 2..4 and batches
+    that do not divide evenly (or are smaller than n)."""
     from vdttfs import engine as E
     net, layers, img = _net_case(name, B, 3 if name == "vgg16" else 1, 0.0 if name == "vgg16" else 0.8)
     spikes = O.encode_linear(img, net.T)
     ref = O.run_net(net, layers, spikes)
     m = E.Model(net, layers, lut_source=E.LUT_HOST_LIBM)
     ctx = E.Context(m, B)
-    ctx.set_sub_batches(2)
-    for graphs in (True, False):
-        ctx.set_graphs(graphs)
-        out, pred = ctx.infer(_t(spikes, dev))
-        _sync()
-        assert bits_equal(_np(out), ref["out"]) and np.array_equal(_np(pred), ref["pred"]), f"graphs={graphs}"
-    outs, preds = ctx.infer_host_batches([spikes, spikes])
-    assert all(bits_equal(o, ref["out"]) for o in outs) and all(np.array_equal(p, ref["pred"]) for p in preds)
+    for n in (2, 3, 4):
+        ctx.set_sub_batches(n)
+        for graphs in (True, False):
+            ctx.set_graphs(graphs)
+            out, pred = ctx.infer(_t(spikes, dev))
+            _sync()
+            assert bits_equal(_np(out), ref["out"]) and np.array_equal(_np(pred), ref["pred"]), f"n={n} graphs={graphs}"
+        outs, preds = ctx.infer_host_batches([spikes, spikes])
+        assert all(bits_equal(o, ref["out"]) for o in outs) and all(np.array_equal(p, ref["pred"]) for p in preds)
     ctx.set_counting(True)                                   # counting passes run whole batches
     out, _ = ctx.infer(_t(spikes, dev))
     _sync()
     assert bits_equal(_np(out), ref["out"])
     with pytest.raises(E.VdtError):
-        ctx.set_sub_batches(3)
+        ctx.set_sub_batches(5)
     ctx.close()
     m.close()
 

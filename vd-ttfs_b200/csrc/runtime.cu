@@ -195,15 +195,19 @@ struct vdt_ctx {
     int32_t* pred_slot2 = nullptr;
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_h2d[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
-    // sub-batches (vdt_ctx_set_sub_batches): the second half of a batch runs
-    // on sub_stream with its own activation and bucket workspace
+    // sub-batches (vdt_ctx_set_sub_batches): parts 1.. of a batch run on
+    // their own streams with their own activation and bucket workspaces
+    struct SubWs {
+        float* act[3] = {nullptr, nullptr, nullptr};
+        int* off = nullptr;
+        int* cin = nullptr;
+        float* tin = nullptr;
+        cudaStream_t stream = nullptr;
+        cudaEvent_t join = nullptr;
+    };
     int n_sub = 1;
-    float* act2[3] = {nullptr, nullptr, nullptr};
-    int* off2 = nullptr;
-    int* cin2 = nullptr;
-    float* tin2 = nullptr;
-    cudaStream_t sub_stream = nullptr;
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    std::vector<SubWs> sub;                  // n_sub - 1 entries once made
+    cudaEvent_t ev_fork = nullptr;
     int* off = nullptr;
     int* cin = nullptr;
     float* tin = nullptr;
@@ -503,11 +507,14 @@ void ctx_free(vdt_ctx* c) {
         if (c->ev_done[i]) cudaEventDestroy(c->ev_done[i]);
     }
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
-    for (auto& a : c->act2) cudaFree(a);
-    cudaFree(c->off2); cudaFree(c->cin2); cudaFree(c->tin2);
+    for (auto& w : c->sub) {
+        for (auto& a : w.act) cudaFree(a);
+        cudaFree(w.off); cudaFree(w.cin); cudaFree(w.tin);
+        if (w.join) cudaEventDestroy(w.join);
+        if (w.stream) cudaStreamDestroy(w.stream);
+    }
+    c->sub.clear();
     if (c->ev_fork) cudaEventDestroy(c->ev_fork);
-    if (c->ev_join) cudaEventDestroy(c->ev_join);
-    if (c->sub_stream) cudaStreamDestroy(c->sub_stream);
     cudaFree(c->off); cudaFree(c->cin); cudaFree(c->tin); cudaFree(c->counters);
 }
 
@@ -608,36 +615,45 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
     return VDT_OK;
 }
 
-// One batch, split in two halves on two streams when sub-batches are on (the
-// first half on the ctx stream, the second on sub_stream with the second
-// workspace; each half is an independent run of the same per-batch body, so
+// One batch, split into n_sub parts on n_sub streams when sub-batches are
+// on (part 0 on the ctx stream, part k on sub[k - 1]'s stream with its
+// workspace; each part is an independent run of the same per-batch body, so
 // the results are those of one run).  Counting and profiling passes run
 // whole.
 int enqueue_split(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, int32_t* d_pred) {
-    if (c->n_sub < 2 || B < 2 || c->counting || c->profiling)
-        return enqueue(c, d_input, pixels, B, d_out, d_pred, nullptr);
+    const int n = std::min(c->n_sub, B);
+    if (n < 2 || c->counting || c->profiling) return enqueue(c, d_input, pixels, B, d_out, d_pred, nullptr);
     const vdt_model* m = c->m;
-    const int b1 = (B + 1) / 2, b2 = B - b1;
     const size_t in_row = (size_t)m->net.in_h * m->net.in_w * m->net.in_c;
     cudaStream_t s = c->stream;
     VDT_CUDA(cudaEventRecord(c->ev_fork, s));
-    VDT_CUDA(cudaStreamWaitEvent(c->sub_stream, c->ev_fork, 0));
-    if (int st = enqueue(c, d_input, pixels, b1, d_out, d_pred, nullptr)) return st;
-    // the second half: the ctx's stream and workspace swapped for the second set
-    auto swap_ws = [c] {
-        std::swap(c->stream, c->sub_stream);
-        for (int i = 0; i < 3; ++i) std::swap(c->act[i], c->act2[i]);
-        std::swap(c->off, c->off2);
-        std::swap(c->cin, c->cin2);
-        std::swap(c->tin, c->tin2);
+    auto swap_ws = [c](vdt_ctx::SubWs& w) {
+        std::swap(c->stream, w.stream);
+        for (int i = 0; i < 3; ++i) std::swap(c->act[i], w.act[i]);
+        std::swap(c->off, w.off);
+        std::swap(c->cin, w.cin);
+        std::swap(c->tin, w.tin);
     };
-    swap_ws();
-    const int st = enqueue(c, d_input + (size_t)b1 * in_row, pixels, b2, d_out + (size_t)b1 * m->n_classes,
-                           d_pred ? d_pred + b1 : nullptr, nullptr);
-    swap_ws();
-    if (st) return st;
-    VDT_CUDA(cudaEventRecord(c->ev_join, c->sub_stream));
-    VDT_CUDA(cudaStreamWaitEvent(s, c->ev_join, 0));
+    int b0 = 0;
+    for (int k = 0; k < n; ++k) {
+        const int bk = B / n + (k < B % n ? 1 : 0);
+        const float* in = d_input + (size_t)b0 * in_row;
+        float* out = d_out + (size_t)b0 * m->n_classes;
+        int32_t* pred = d_pred ? d_pred + b0 : nullptr;
+        if (k == 0) {
+            if (int st = enqueue(c, in, pixels, bk, out, pred, nullptr)) return st;
+        } else {
+            vdt_ctx::SubWs& w = c->sub[k - 1];
+            VDT_CUDA(cudaStreamWaitEvent(w.stream, c->ev_fork, 0));
+            swap_ws(w);
+            const int st = enqueue(c, in, pixels, bk, out, pred, nullptr);
+            swap_ws(w);
+            if (st) return st;
+            VDT_CUDA(cudaEventRecord(w.join, w.stream));
+            VDT_CUDA(cudaStreamWaitEvent(s, w.join, 0));
+        }
+        b0 += bk;
+    }
     return VDT_OK;
 }
 
@@ -646,21 +662,21 @@ int enqueue_split(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_
 extern "C" int vdt_ctx_set_sub_batches(vdt_ctx* c, int n) {
     g_last_error.clear();
     if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
-    if (n != 1 && n != 2) return fail(VDT_ERR_INVALID, "n=%d (1 or 2)", n);
+    if (n < 1 || n > VDT_MAX_SUB_BATCHES) return fail(VDT_ERR_INVALID, "n=%d (1 to %d)", n, VDT_MAX_SUB_BATCHES);
     DeviceGuard g(c->m->device);
-    if (n == 2 && !c->sub_stream) {
-        const Sizes z = ctx_sizes(c->m, (c->max_batch + 1) / 2);
+    if (!c->ev_fork) VDT_CUDA(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
+    const Sizes z = ctx_sizes(c->m, (c->max_batch + n - 1) / n);
+    while ((int)c->sub.size() < n - 1) {                     // workspaces made once, kept
+        vdt_ctx::SubWs w;
         cudaError_t e = cudaSuccess;
-        for (auto& a : c->act2) if (e == cudaSuccess) e = cudaMalloc(&a, z.act * sizeof(float));
-        if (e == cudaSuccess) e = cudaMalloc(&c->off2, std::max<size_t>(z.off, 1) * sizeof(int));
-        if (e == cudaSuccess) e = cudaMalloc(&c->cin2, std::max<size_t>(z.bkt, 1) * sizeof(int));
-        if (e == cudaSuccess) e = cudaMalloc(&c->tin2, std::max<size_t>(z.bkt, 1) * sizeof(float));
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming);
-        cudaStream_t ss = nullptr;
-        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ss, cudaStreamNonBlocking);
+        for (auto& a : w.act) if (e == cudaSuccess) e = cudaMalloc(&a, z.act * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&w.off, std::max<size_t>(z.off, 1) * sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&w.cin, std::max<size_t>(z.bkt, 1) * sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&w.tin, std::max<size_t>(z.bkt, 1) * sizeof(float));
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&w.join, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&w.stream, cudaStreamNonBlocking);
+        c->sub.push_back(w);                                 // freed with the ctx, even on failure
         if (e != cudaSuccess) return cuda_fail(e, "sub-batch workspace");
-        c->sub_stream = ss;
     }
     if (c->n_sub != n) {
         VDT_CUDA(cudaStreamSynchronize(c->stream));
