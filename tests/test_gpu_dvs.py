@@ -142,6 +142,27 @@ def test_pool_chunk_early(O, dev, layout):
     assert np.mean(ref < INF) > 0.05
 
 
+@pytest.mark.parametrize("th", [0.0, 1.0, 2.5, 5.0])
+def test_pool_chunk_early_thresholds(O, dev, th):
+    """The pool's scan starts at the chunk of the earliest input spike when
+    th > 0 (I and V are exactly 0 before it); th = 0 fires every neuron at
+    step 0 through the full scan; sparse inputs leave neurons without any
+    spike, T not a multiple of delta makes the scan run past T."""
+    import dataclasses
+    from vdttfs import dvs, nets
+    spec = dataclasses.replace(nets.dvs_ref(T=150, delta=32), th_conv=th)
+    rng = np.random.default_rng(int(th * 10) + 7)
+    N, Cc, H, W = 2, 24, 10, 8
+    x = spike_map(rng, (N, Cc, H, W), fire=0.15, T=spec.T, edges=True)
+    ref = O.dvs_pool(x, N, Cc, H, W, spec)
+    got = _np(dvs.pool(_t(x, dev), N, Cc, H, W, spec))
+    assert bits_equal(got, ref)
+    if th == 0.0:
+        assert np.all(ref == 0.0)
+    else:
+        assert 0.0 < np.mean(ref < INF) < 1.0
+
+
 def test_fc1_recurrent_and_fc2(O, dev):
     from vdttfs import dvs, nets, synth
     spec = nets.dvs_ref()

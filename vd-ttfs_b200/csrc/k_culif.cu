@@ -135,7 +135,18 @@ __global__ void k_culif_pool(const float* __restrict__ in, float* __restrict__ o
             tf[d] = __ldg(in + at);
         }
         float I = 0.0f, V = 0.0f, res = 9999.0f;
-        for (int tau = 0; tau < NC; ++tau) {
+        // before the first input spike I and V stay exactly 0 (fma(0, d, 0) = 0,
+        // 0 + 0 = 0), so with th > 0 nothing can fire there: start at the
+        // chunk holding the earliest spike of the scan (none: never fires)
+        int tau0 = 0;
+        if (th > 0.0f) {
+            float tmin = 3.0e38f;
+#pragma unroll
+            for (int d = 0; d < 4; ++d)
+                if (tf[d] >= 0.0f && tf[d] < (float)(NC * delta)) tmin = fminf(tmin, tf[d]);
+            tau0 = tmin < 3.0e38f ? (int)tmin / delta : NC;
+        }
+        for (int tau = tau0; tau < NC; ++tau) {
             const int base = tau * delta;
             unsigned long long set = 0;                      // bins of this chunk holding a spike
 #pragma unroll
