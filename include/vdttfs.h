@@ -299,6 +299,19 @@ int vdt_dvs_pool(const float* d_in, float* d_out, int N, int C, int H_in, int W_
 int vdt_dvs_fc1_recurrent(const int* d_off, const int* d_cin, const float* d_tin,
                           const float* d_w_t, const float* d_wrec_t, int N, int F_in, int F_out,
                           int T, int delta, float decay, float th, float* d_out, vdt_stream stream);
+/* Where F_out is a multiple of 128, the feed-forward sums of every
+   (sample, step, neuron) are built first by an event-parallel kernel into a
+   scratch buffer of vdt_dvs_fc1_scratch_bytes(N, F_out, T, delta) bytes (0:
+   none used for this shape); vdt_dvs_fc1_recurrent allocates it
+   stream-ordered per call, vdt_dvs_fc1_recurrent_ws takes it from the caller
+   (device memory, 16-byte aligned; VDT_ERR_CAPACITY when smaller).  Same
+   results either way.  No reference counterpart (the reference sums each
+   neuron's events inside the recurrent kernel). */
+size_t vdt_dvs_fc1_scratch_bytes(int N, int F_out, int T, int delta);
+int vdt_dvs_fc1_recurrent_ws(const int* d_off, const int* d_cin, const float* d_tin,
+                             const float* d_w_t, const float* d_wrec_t, int N, int F_in, int F_out,
+                             int T, int delta, float decay, float th, float* d_out, void* d_scratch,
+                             size_t scratch_bytes, vdt_stream stream);
 
 /* fc2_bucketed_early (t3:203-225): bucketed FC, transposed weights
    d_w_t[j][i] = W_fc2[i][j] ([F_in, F_out]); output [N, F_out]. */

@@ -163,18 +163,26 @@ def test_pool_chunk_early_thresholds(O, dev, th):
         assert 0.0 < np.mean(ref < INF) < 1.0
 
 
-def test_fc1_recurrent_and_fc2(O, dev):
+@pytest.mark.parametrize("F_out", [128, 96, 256])
+def test_fc1_recurrent_and_fc2(O, dev, F_out):
+    """FC1 (feed-forward sums event-parallel in k_fc1_ff when F_out is a
+    multiple of 128, else per neuron inside the recurrent kernel) and FC2
+    against the oracle, bit for bit."""
     from vdttfs import dvs, nets, synth
     spec = nets.dvs_ref()
-    rng = np.random.default_rng(11)
-    N, F_in, F_out, K = 5, 700, 128, 11
+    rng = np.random.default_rng(11 + F_out)
+    N, F_in, K = 5, 700, 11
     x = spike_map(rng, (N, F_in), fire=0.3, T=spec.T, edges=True)
     w = (rng.standard_normal((F_out, F_in)) * 0.25).astype(np.float32)
     wr = (rng.standard_normal((F_out, F_out)) * 0.5).astype(np.float32)
     ref1, _ = O.dvs_fc1(x, w, wr, N, F_in, F_out, spec)
     b = dvs.bucketize_rows(_t(x, dev), N, F_in, spec)
-    got1 = _np(dvs.fc1_recurrent(b, _t(w.T, dev), _t(wr.T, dev), N, F_in, F_out, spec))
-    assert bits_equal(got1, ref1)
+    for ws in (True, False):                                 # caller's scratch / library's own
+        got1 = _np(dvs.fc1_recurrent(b, _t(w.T, dev), _t(wr.T, dev), N, F_in, F_out, spec, workspace=ws))
+        assert bits_equal(got1, ref1), f"workspace={ws}"
+    from vdttfs._lib import lib
+    need = lib().vdt_dvs_fc1_scratch_bytes(N, F_out, spec.T, spec.delta)
+    assert (need > 0) == (F_out % 128 == 0)
     assert 0.0 < np.mean(ref1 < INF) < 1.0
     w2 = (rng.standard_normal((K, F_out)) * 0.8).astype(np.float32)
     ref2, fe, _ = O.dvs_fc2(ref1, w2, N, F_out, K, spec)

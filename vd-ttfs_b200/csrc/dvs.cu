@@ -1,4 +1,6 @@
 // dvs.cu -- C entry points of the task-3 (DVS gesture, CuLIF) stages.
+#include <cstdio>
+
 #include "vdt_internal.h"
 
 using namespace vdt;
@@ -106,18 +108,53 @@ extern "C" int vdt_dvs_pool(const float* d_in, float* d_out, int N, int C, int H
                        "pool_chunk_early launch");
 }
 
-extern "C" int vdt_dvs_fc1_recurrent(const int* d_off, const int* d_cin, const float* d_tin, const float* d_w_t,
-                                     const float* d_wrec_t, int N, int F_in, int F_out, int T, int delta,
-                                     float decay, float th, float* d_out, vdt_stream stream) {
-    api_clear_error();
+namespace {
+int fc1_checks(const int* d_off, const int* d_cin, const float* d_tin, const float* d_w_t, const float* d_wrec_t,
+               int N, int F_in, int F_out, int T, int delta, const float* d_out) {
     if (!d_off || !d_cin || !d_tin || !d_w_t || !d_wrec_t || !d_out || N < 0 || F_in <= 0 || F_out <= 0 ||
         !culif_ok(T, delta))
         return api_fail(VDT_ERR_INVALID, "bad fc1_bucketed_recurrent arguments");
     if (F_out % 32 != 0 || F_out > 1024)
         return api_fail(VDT_ERR_UNSUPPORTED, "F_out must be a multiple of 32, at most 1024");
+    return VDT_OK;
+}
+}  // namespace
+
+extern "C" int vdt_dvs_fc1_recurrent(const int* d_off, const int* d_cin, const float* d_tin, const float* d_w_t,
+                                     const float* d_wrec_t, int N, int F_in, int F_out, int T, int delta,
+                                     float decay, float th, float* d_out, vdt_stream stream) {
+    api_clear_error();
+    if (int st = fc1_checks(d_off, d_cin, d_tin, d_w_t, d_wrec_t, N, F_in, F_out, T, delta, d_out)) return st;
     if (int s = api_check_buffers(-1, {d_off, d_cin, d_tin, d_w_t, d_wrec_t, d_out})) return s;
     return cuda_status(launch_culif_fc1_rec(d_off, d_cin, d_tin, d_w_t, d_wrec_t, d_out, N, F_in, F_out, T, delta,
-                                            decay, th, static_cast<cudaStream_t>(stream)),
+                                            decay, th, static_cast<cudaStream_t>(stream), nullptr),
+                       "fc1_bucketed_recurrent launch");
+}
+
+extern "C" size_t vdt_dvs_fc1_scratch_bytes(int N, int F_out, int T, int delta) {
+    return culif_fc1_scratch_bytes(N, F_out, T, delta);
+}
+
+extern "C" int vdt_dvs_fc1_recurrent_ws(const int* d_off, const int* d_cin, const float* d_tin, const float* d_w_t,
+                                        const float* d_wrec_t, int N, int F_in, int F_out, int T, int delta,
+                                        float decay, float th, float* d_out, void* d_scratch, size_t scratch_bytes,
+                                        vdt_stream stream) {
+    api_clear_error();
+    if (int st = fc1_checks(d_off, d_cin, d_tin, d_w_t, d_wrec_t, N, F_in, F_out, T, delta, d_out)) return st;
+    const size_t need = culif_fc1_scratch_bytes(N, F_out, T, delta);
+    if (need > 0 && (!d_scratch || scratch_bytes < need)) {
+        char msg[160];
+        snprintf(msg, sizeof(msg), "scratch of %zu bytes, the call needs %zu (vdt_dvs_fc1_scratch_bytes)",
+                 scratch_bytes, need);
+        return api_fail(VDT_ERR_CAPACITY, msg);
+    }
+    if (need > 0 && (reinterpret_cast<uintptr_t>(d_scratch) & 15))
+        return api_fail(VDT_ERR_INVALID, "d_scratch must be 16-byte aligned");
+    if (int s = api_check_buffers(-1, {d_off, d_cin, d_tin, d_w_t, d_wrec_t, d_out, need ? d_scratch : nullptr}))
+        return s;
+    return cuda_status(launch_culif_fc1_rec(d_off, d_cin, d_tin, d_w_t, d_wrec_t, d_out, N, F_in, F_out, T, delta,
+                                            decay, th, static_cast<cudaStream_t>(stream),
+                                            need ? static_cast<float*>(d_scratch) : nullptr),
                        "fc1_bucketed_recurrent launch");
 }
 

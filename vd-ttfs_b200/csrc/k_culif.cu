@@ -173,10 +173,69 @@ __global__ void k_culif_pool(const float* __restrict__ in, float* __restrict__ o
 // j), I = fma(I, decay, in_ff) + in_rec, V += I; a neuron fires once and
 // its V is reset to -10000.  No early exit.  Weights are transposed:
 // w_t[j][i] = W_fc1[i][j], wrec_t[j][i] = W_rec[i][j].
+// FC1's feed-forward input, event-parallel: one warp per (sample, step,
+// group of 128 neurons), lane l owns neurons 4l..4l+3 of the group and sums
+// them in registers.  The warp scans its chunk's bucket list 32 events at a
+// time and takes the events of its own step (ballot, lowest lane first), so
+// per (step, neuron) the additions run in bucket order: the reference's
+// in_ff[tt - base] += w chain (t3:186).  Up to 8 weight rows load at once.
+// Output ff[n][t][i] for t < NC * delta.
+constexpr int FF_WARPS = 4;
+
+__global__ void __launch_bounds__(FF_WARPS * 32) k_fc1_ff(const int* __restrict__ off, const int* __restrict__ bcin,
+                                                          const float* __restrict__ btin,
+                                                          const float* __restrict__ w_t, float* __restrict__ ff,
+                                                          int N, int F_in, int F_out, int delta, int NC) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = F_out / 128, TS = NC * delta;
+    const long long item = (long long)blockIdx.x * FF_WARPS + warp;
+    if (item >= (long long)N * TS * G) return;               // warp-uniform
+    const int g = (int)(item % G);
+    const int t = (int)((item / G) % TS);
+    const long long n = item / ((long long)G * TS);
+    const int ch = t / delta, OS = NC + 1;
+    const int s = __ldg(off + n * OS + ch), e = __ldg(off + n * OS + ch + 1);
+    const int* sc = bcin + n * F_in;
+    const float* st = btin + n * F_in;
+    const float* wl = w_t + g * 128 + lane * 4;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int p0 = s; p0 < e; p0 += 32) {
+        int j = 0;
+        bool mine = false;
+        if (p0 + lane < e) {
+            j = __ldg(sc + p0 + lane);
+            mine = (int)__ldg(st + p0 + lane) == t;
+        }
+        unsigned m = __ballot_sync(FULL_MASK, mine);
+        while (m) {                                          // warp-uniform
+            float4 w[8];
+            int cnt = 0;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (m) {
+                    const int b = __ffs(m) - 1;
+                    m &= m - 1;
+                    const int jq = __shfl_sync(FULL_MASK, j, b);
+                    w[u] = __ldg(reinterpret_cast<const float4*>(wl + (long long)jq * F_out));
+                    cnt = u + 1;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (u < cnt) { acc.x += w[u].x; acc.y += w[u].y; acc.z += w[u].z; acc.w += w[u].w; }
+            }
+        }
+    }
+    *reinterpret_cast<float4*>(ff + (n * TS + t) * F_out + g * 128 + lane * 4) = acc;
+}
+
+// With ff (k_fc1_ff's feed-forward sums) each chunk reads those sums;
+// without, each neuron sums its own events.
 __global__ void k_culif_fc1_rec(const int* __restrict__ off, const int* __restrict__ bcin,
                                 const float* __restrict__ btin, const float* __restrict__ w_t,
-                                const float* __restrict__ wrec_t, float* __restrict__ out, int F_in,
-                                int F_out, int delta, int NC, float decay, float th) {
+                                const float* __restrict__ wrec_t, const float* __restrict__ ff,
+                                float* __restrict__ out, int F_in, int F_out, int delta, int NC, float decay,
+                                float th) {
     extern __shared__ float f1_sm[];
     float* s_ff = f1_sm;                                     // [delta][F_out]
     unsigned* s_prev = reinterpret_cast<unsigned*>(s_ff + (size_t)delta * F_out);   // fired bitmap
@@ -191,12 +250,17 @@ __global__ void k_culif_fc1_rec(const int* __restrict__ off, const int* __restri
     const float* st = btin + n * F_in;
     for (int ch = 0; ch < NC; ++ch) {
         const int base = ch * delta;
-        for (int t = 0; t < delta; ++t) s_ff[t * F_out + i] = 0.0f;
-        const int s = __ldg(off + n * OS + ch), e = __ldg(off + n * OS + ch + 1);
-        for (int p = s; p < e; ++p) {
-            const int j = __ldg(sc + p);
-            const int tt = (int)__ldg(st + p);
-            s_ff[(tt - base) * F_out + i] += __ldg(w_t + (long long)j * F_out + i);
+        if (ff) {
+            const float* fr = ff + (n * NC * delta + base) * F_out + i;
+            for (int t = 0; t < delta; ++t) s_ff[t * F_out + i] = __ldg(fr + (long long)t * F_out);
+        } else {
+            for (int t = 0; t < delta; ++t) s_ff[t * F_out + i] = 0.0f;
+            const int s = __ldg(off + n * OS + ch), e = __ldg(off + n * OS + ch + 1);
+            for (int p = s; p < e; ++p) {
+                const int j = __ldg(sc + p);
+                const int tt = (int)__ldg(st + p);
+                s_ff[(tt - base) * F_out + i] += __ldg(w_t + (long long)j * F_out + i);
+            }
         }
         for (int t = 0; t < delta; ++t) {
             __syncthreads();                                 // previous step's bitmap complete
@@ -295,9 +359,15 @@ cudaError_t launch_culif_pool(const float* in, float* out, int N, int C, int H_i
     return cudaGetLastError();
 }
 
+size_t culif_fc1_scratch_bytes(int N, int F_out, int T, int delta) {
+    if (N <= 0 || F_out % 128 != 0 || delta < 1) return 0;
+    const int NC = (T + delta - 1) / delta;
+    return (size_t)N * NC * delta * F_out * sizeof(float);
+}
+
 cudaError_t launch_culif_fc1_rec(const int* off, const int* cin, const float* tin, const float* w_t,
                                  const float* wrec_t, float* out, int N, int F_in, int F_out, int T, int delta,
-                                 float decay, float th, cudaStream_t s) {
+                                 float decay, float th, cudaStream_t s, float* scratch) {
     if (F_out < 1 || F_out > 1024 || F_out % 32 != 0 || delta < 1) return cudaErrorInvalidValue;
     if (N <= 0) return cudaSuccess;
     const int NC = (T + delta - 1) / delta;
@@ -307,8 +377,39 @@ cudaError_t launch_culif_fc1_rec(const int* off, const int* cin, const float* ti
         cudaError_t e = cudaFuncSetAttribute(k_culif_fc1_rec, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    k_culif_fc1_rec<<<N, F_out, smem, s>>>(off, cin, tin, w_t, wrec_t, out, F_in, F_out, delta, NC, decay, th);
-    return cudaGetLastError();
+    // feed-forward sums first, event-parallel, where the neurons split into
+    // groups of 128 and the per-warp step table fits: into the caller's
+    // scratch, else a stream-ordered allocation freed after the launch
+    float* ff = nullptr;
+    bool own = false;
+    if (culif_fc1_scratch_bytes(N, F_out, T, delta) > 0) {
+        cudaError_t e = cudaSuccess;
+        if (scratch) {
+            ff = scratch;
+        } else {
+            e = cudaMallocAsync(&ff, culif_fc1_scratch_bytes(N, F_out, T, delta), s);
+            if (e != cudaSuccess) return e;
+            own = true;
+        }
+        const long long items = (long long)N * NC * delta * (F_out / 128);
+        if ((items + FF_WARPS - 1) / FF_WARPS >= (1ll << 31)) e = cudaErrorInvalidValue;
+        if (e == cudaSuccess) {
+            k_fc1_ff<<<(unsigned)((items + FF_WARPS - 1) / FF_WARPS), FF_WARPS * 32, 0, s>>>(
+                off, cin, tin, w_t, ff, N, F_in, F_out, delta, NC);
+            e = cudaGetLastError();
+        }
+        if (e != cudaSuccess) {
+            if (own) cudaFreeAsync(ff, s);
+            return e;
+        }
+    }
+    k_culif_fc1_rec<<<N, F_out, smem, s>>>(off, cin, tin, w_t, wrec_t, ff, out, F_in, F_out, delta, NC, decay, th);
+    cudaError_t e = cudaGetLastError();
+    if (own) {
+        const cudaError_t e2 = cudaFreeAsync(ff, s);
+        if (e == cudaSuccess) e = e2;
+    }
+    return e;
 }
 
 cudaError_t launch_oihw_to_hwio(const float* src, float* dst, int O, int I, int K, cudaStream_t s) {

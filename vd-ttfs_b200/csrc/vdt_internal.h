@@ -123,9 +123,12 @@ cudaError_t launch_culif_conv1(const float* frames, const float* w_oihw, float* 
                                int H, int W, int K, int T, int delta, float decay, float th, cudaStream_t s);
 cudaError_t launch_culif_pool(const float* in, float* out, int N, int C, int H_in, int W_in, int layout,
                               int T, int delta, float decay, float th, cudaStream_t s);
+// scratch: the feed-forward sums' buffer (culif_fc1_scratch_bytes; 0 = not
+// used for this shape); NULL allocates it stream-ordered
 cudaError_t launch_culif_fc1_rec(const int* off, const int* cin, const float* tin, const float* w_t,
                                  const float* wrec_t, float* out, int N, int F_in, int F_out, int T, int delta,
-                                 float decay, float th, cudaStream_t s);
+                                 float decay, float th, cudaStream_t s, float* scratch);
+size_t culif_fc1_scratch_bytes(int N, int F_out, int T, int delta);
 cudaError_t launch_oihw_to_hwio(const float* src, float* dst, int O, int I, int K, cudaStream_t s);
 bool sorted_supported(int K, int is_fc, int delta, int C_in, int C_out, int T, int decay_len);
 

@@ -83,6 +83,9 @@ SIGNATURES = {
                            [C.c_float, C.c_float, C.c_int, _vp, _vp]),
     "vdt_dvs_pool": (C.c_int, [_vp, _vp] + [C.c_int] * 7 + [C.c_float, C.c_float, _vp]),
     "vdt_dvs_fc1_recurrent": (C.c_int, [_vp] * 5 + [C.c_int] * 5 + [C.c_float, C.c_float, _vp, _vp]),
+    "vdt_dvs_fc1_scratch_bytes": (C.c_size_t, [C.c_int] * 4),
+    "vdt_dvs_fc1_recurrent_ws": (C.c_int, [_vp] * 5 + [C.c_int] * 5 + [C.c_float, C.c_float, _vp, _vp,
+                                                                       C.c_size_t, _vp]),
     "vdt_dvs_fc2": (C.c_int, [_vp] * 4 + [C.c_int] * 5 + [C.c_float, C.c_float, _vp, _vp]),
     "vdt_oihw_to_hwio": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, _vp]),
     "vdt_set_launch_overlap": (C.c_int, [C.c_int]),

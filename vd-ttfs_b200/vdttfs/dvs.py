@@ -120,13 +120,22 @@ def pool(x, N, Cc, H, W, spec, layout=LAYOUT_NCHW, stream=None):
     return out
 
 
-def fc1_recurrent(buckets, w_t, rec_t, N, F_in, F_out, spec, stream=None):
+def fc1_recurrent(buckets, w_t, rec_t, N, F_in, F_out, spec, stream=None, workspace=True):
+    """fc1_bucketed_recurrent.  workspace=True hands the feed-forward sums'
+    scratch over from torch's caching allocator (vdt_dvs_fc1_recurrent_ws);
+    False lets the library allocate it stream-ordered per call."""
     import torch
     off, cin, tin = buckets
     out = torch.empty((N * F_out,), dtype=torch.float32, device=off.device)
-    check(lib().vdt_dvs_fc1_recurrent(_ptr(off), _ptr(cin), _ptr(tin), _ptr(w_t), _ptr(rec_t), N, F_in, F_out,
-                                      spec.T, spec.delta, spec.decay_fc, spec.th_fc, _ptr(out),
-                                      C.c_void_p(_stream(stream))), "vdt_dvs_fc1_recurrent")
+    args = (_ptr(off), _ptr(cin), _ptr(tin), _ptr(w_t), _ptr(rec_t), N, F_in, F_out,
+            spec.T, spec.delta, spec.decay_fc, spec.th_fc, _ptr(out))
+    if workspace:
+        nbytes = lib().vdt_dvs_fc1_scratch_bytes(N, F_out, spec.T, spec.delta)
+        ws = torch.empty((max(nbytes, 4) // 4,), dtype=torch.float32, device=off.device)
+        check(lib().vdt_dvs_fc1_recurrent_ws(*args, _ptr(ws), nbytes, C.c_void_p(_stream(stream))),
+              "vdt_dvs_fc1_recurrent_ws")
+    else:
+        check(lib().vdt_dvs_fc1_recurrent(*args, C.c_void_p(_stream(stream))), "vdt_dvs_fc1_recurrent")
     return out
 
 
