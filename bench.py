@@ -714,6 +714,7 @@ def sweep_point(E, nets, synth, dev, delta, zf, T, B, steps, warmup, flush):
     img = synth.images(5, B, net.in_h, net.in_w, net.in_c, zf)
     model = E.Model(net, layers, device=dev.index)
     ctx = E.Context(model, B)
+    ctx.set_sub_batches(2)      # as the main workload
     x = torch.from_numpy(img).to(dev)
     ctx.set_counting(True)
     ctx.infer(x, pixels=True)
