@@ -201,20 +201,49 @@ struct CulifLanes {
         res[v] = fire ? (float)s : res[v];
         alive[v] = alive[v] && !fire;
     }
-    // step s with input acc (the step's in[] sum), then acc = 0
-    __device__ __forceinline__ void close_step_bf(int s, const CulifCfg& c) {
+    // step s of every channel with inputs in[]: channel pairs update I and V
+    // with packed fma.rn.f32x2 / add.rn.f32x2 (two independent
+    // round-to-nearest operations, the same results as fmaf and +)
+    __device__ __forceinline__ void step_all(int s, const float (&in)[V], const CulifCfg& c) {
+#pragma unroll
+        for (int v = 0; v + 1 < V; v += 2) {
+            asm("{\n\t"
+                ".reg .b64 i, d, x, m;\n\t"
+                "mov.b64 i, {%0, %1};\n\t"
+                "mov.b64 d, {%4, %4};\n\t"
+                "mov.b64 x, {%5, %6};\n\t"
+                "fma.rn.f32x2 i, i, d, x;\n\t"
+                "mov.b64 m, {%2, %3};\n\t"
+                "add.rn.f32x2 m, m, i;\n\t"
+                "mov.b64 {%0, %1}, i;\n\t"
+                "mov.b64 {%2, %3}, m;\n\t"
+                "}"
+                : "+f"(I[v]), "+f"(I[v + 1]), "+f"(Vm[v]), "+f"(Vm[v + 1])
+                : "f"(c.decay), "f"(in[v]), "f"(in[v + 1]));
+        }
+        if constexpr (V % 2 == 1) {
+            I[V - 1] = fmaf(I[V - 1], c.decay, in[V - 1]);
+            Vm[V - 1] += I[V - 1];
+        }
 #pragma unroll
         for (int v = 0; v < V; ++v) {
-            step(s, acc[v], v, c);
-            acc[v] = 0.0f;
+            const bool fire = alive[v] && Vm[v] >= c.th;
+            res[v] = fire ? (float)s : res[v];
+            alive[v] = alive[v] && !fire;
         }
+    }
+    // step s with input acc (the step's in[] sum), then acc = 0
+    __device__ __forceinline__ void close_step_bf(int s, const CulifCfg& c) {
+        step_all(s, acc, c);
+#pragma unroll
+        for (int v = 0; v < V; ++v) acc[v] = 0.0f;
     }
     // steps [a, b) without input
     __device__ __forceinline__ void close_empty(int a, int b, const CulifCfg& c) {
-        for (int t = a; t < b; ++t) {
+        float zero[V];
 #pragma unroll
-            for (int v = 0; v < V; ++v) step(t, 0.0f, v, c);
-        }
+        for (int v = 0; v < V; ++v) zero[v] = 0.0f;
+        for (int t = a; t < b; ++t) step_all(t, zero, c);
     }
 };
 
