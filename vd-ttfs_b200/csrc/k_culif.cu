@@ -67,17 +67,20 @@ __global__ void __launch_bounds__(C1_WARPS * 32) k_culif_conv1(const float* __re
     const float* fpix = frames + ((n * C_in * H + y) * (long long)W + x) * T;
     for (int tau = 0; tau < NC; ++tau) {
         const int base = tau * DELTA;
+        // lane l stages bin l % DELTA of taps l / DELTA, l / DELTA + 32 / DELTA, ...
+        // and marks the nonzero ones; OR over the lanes of one bin gives its mask
+        unsigned mask = 0;                                    // lane t: taps with input in bin t
         for (int i = lane; i < taps * DELTA; i += 32) {
             const int q = i / DELTA, t = i - q * DELTA;      // DELTA is a power of two
             float v = 0.0f;
             if ((unsigned)(y + s_tdy[q]) < (unsigned)H && (unsigned)(x + s_tdx[q]) < (unsigned)W && base + t < T)
                 v = __ldg(fpix + s_toff[q] + base + t);
             s_f[i] = v;
+            mask |= (v != 0.0f ? 1u : 0u) << q;
         }
+#pragma unroll
+        for (int o = DELTA; o < 32; o <<= 1) mask |= __shfl_xor_sync(FULL_MASK, mask, o);
         __syncwarp();
-        unsigned mask = 0;                                    // lane t: taps with input in bin t
-        if (lane < DELTA)
-            for (int q = 0; q < taps; ++q) mask |= (s_f[q * DELTA + lane] != 0.0f ? 1u : 0u) << q;
 #pragma unroll 4
         for (int t = 0; t < DELTA; ++t) {
             unsigned m = __shfl_sync(FULL_MASK, mask, t);
@@ -91,8 +94,7 @@ __global__ void __launch_bounds__(C1_WARPS * 32) k_culif_conv1(const float* __re
 #pragma unroll
                 for (int v = 0; v < V; ++v) in[v] = fmaf(wl[q * C_out + v], f, in[v]);
             }
-#pragma unroll
-            for (int v = 0; v < V; ++v) nu.step(base + t, in[v], v, cc);
+            nu.step_all(base + t, in, cc);
         }
         __syncwarp();
         if (!__any_sync(FULL_MASK, nu.any())) break;
