@@ -250,8 +250,8 @@ def run_engine(a):
     h_in = torch.from_numpy(img).pin_memory()
     pipelined = img.nbytes > L2_BYTES
     if pipelined:
-        h_outs = [torch.empty((B, net.n_classes), dtype=torch.float32).pin_memory() for _ in range(a.steps)]
-        h_preds = [torch.empty((B,), dtype=torch.int32).pin_memory() for _ in range(a.steps)]
+        h_outs = [torch.empty((B, net.n_classes), dtype=torch.float32).pin_memory() for _ in range(max(a.steps, 2))]
+        h_preds = [torch.empty((B,), dtype=torch.int32).pin_memory() for _ in range(max(a.steps, 2))]
         ctx.infer_host_batches([h_in] * 2, pixels=True, outs=h_outs[:2], preds=h_preds[:2])   # both slots' graphs
         if world > 1:
             dist.barrier()
@@ -259,7 +259,7 @@ def run_engine(a):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-        ctx.infer_host_batches([h_in] * a.steps, pixels=True, outs=h_outs, preds=h_preds)
+        ctx.infer_host_batches([h_in] * a.steps, pixels=True, outs=h_outs[:a.steps], preds=h_preds[:a.steps])
         with torch.cuda.stream(stream):
             e1.record(stream)
         stream.synchronize()
@@ -586,14 +586,14 @@ def run_dvs_engine(a):
     # (step i+1's frames cross while step i computes); smaller ones step by
     # step through the same call with one batch, the L2 flush between steps.
     h_in = torch.from_numpy(frames).pin_memory()
-    h_outs = [torch.empty((B, spec.classes), dtype=torch.float32).pin_memory() for _ in range(a.steps)]
-    h_preds = [torch.empty((B,), dtype=torch.int32).pin_memory() for _ in range(a.steps)]
+    h_outs = [torch.empty((B, spec.classes), dtype=torch.float32).pin_memory() for _ in range(max(a.steps, 2))]
+    h_preds = [torch.empty((B,), dtype=torch.int32).pin_memory() for _ in range(max(a.steps, 2))]
     dvs.run_host_batches(spec, w, [h_in] * 2, h_outs[:2], h_preds[:2])   # warms the copies
     torch.cuda.synchronize()
     if big:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        dvs.run_host_batches(spec, w, [h_in] * a.steps, h_outs, h_preds)
+        dvs.run_host_batches(spec, w, [h_in] * a.steps, h_outs[:a.steps], h_preds[:a.steps])
         e1.record(stream)
         torch.cuda.synchronize()
         e_times = [e0.elapsed_time(e1)]

@@ -209,6 +209,8 @@ def run_host_batches(spec: nets.DvsSpec, w: DvsWeights, h_frames, outs=None, pre
         outs = [torch.empty((N, spec.classes), dtype=torch.float32).pin_memory() for _ in range(n)]
     if preds is None:
         preds = [torch.empty((N,), dtype=torch.int32).pin_memory() for _ in range(n)]
+    if len(outs) != n or len(preds) != n:
+        raise ValueError(f"{n} batches need {n} outputs and predictions, got {len(outs)} and {len(preds)}")
     comp = torch.cuda.current_stream(dev)
     copy = torch.cuda.Stream(dev)
     slots = [torch.empty(h_frames[0].shape, dtype=torch.float32, device=dev) for _ in range(min(2, n))]

@@ -199,6 +199,8 @@ class Context:
             outs = [np.empty((B, self.model.n_classes), np.float32) for _ in range(n)]
         if preds is None:
             preds = [np.empty((B,), np.int32) for _ in range(n)]
+        if len(outs) != n or len(preds) != n:
+            raise ValueError(f"{n} batches need {n} outputs and predictions, got {len(outs)} and {len(preds)}")
 
         def hp(a):
             return a.ctypes.data if isinstance(a, np.ndarray) else a.data_ptr()
