@@ -4,14 +4,15 @@
 // t2:45-170), bit for bit.
 //
 // A warp of 32 pixels replaces 32 warps of k_dense, which for a 6-channel
-// layer would leave 26 of 32 lanes idle.  The thread reads its pixel's inputs
-// once into registers as keys (step << 18 | input index << 13 | LUT index), so
-// increasing key order is the reference's order: by step, and inside a step
-// by (tap, channel) -- each neuron's FMA chain.  A bitonic network sorts the
-// keys in registers once; the thread then walks its sorted events from its
-// own shared-memory column, adds w[input][c] * LUT to every channel's open
-// step, and closes a step when the next key leaves it (lanes.h closes;
-// input-free steps by bisection).
+// layer would leave 26 of 32 lanes idle.  The thread turns its pixel's events
+// into keys (step << 18 | input index << 13 | LUT index), so increasing key
+// order is the reference's order: by step, and inside a step by (tap,
+// channel) -- each neuron's FMA chain.  Each key is inserted in order into
+// the thread's own shared-memory column as it is made (a pixel has few
+// events; a fully unrolled sorting network was slower, its code overflowing
+// the instruction cache).  The thread then walks its sorted events, adds
+// w[input][c] * LUT to every channel's open step, and closes a step when the
+// next key leaves it (lanes.h closes; input-free steps by bisection).
 #include "lanes.h"
 #include "vdt_internal.h"
 
@@ -19,29 +20,7 @@ namespace vdt {
 namespace {
 
 constexpr int TW = 4;             // warps per CTA
-constexpr int TKEYS = 32;         // inputs per pixel held in registers
-constexpr int KEY_NONE = 0x7fffffff;
-
-// ascending bitonic sort of N keys held in registers (N a power of two;
-// fully unrolled, so every compare-exchange is one min and one max)
-template <int N>
-__device__ __forceinline__ void sort_keys(int (&k)[N]) {
-#pragma unroll
-    for (int size = 2; size <= N; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-#pragma unroll
-            for (int i = 0; i < N; ++i) {
-                const int j = i ^ stride;
-                if (j > i) {
-                    const int a = k[i], b = k[j];
-                    const int lo = min(a, b), hi = max(a, b);
-                    if ((i & size) == 0) { k[i] = lo; k[j] = hi; } else { k[i] = hi; k[j] = lo; }
-                }
-            }
-        }
-    }
-}
+constexpr int TKEYS = 32;         // inputs per pixel at most (keys per thread column)
 
 template <int CO, int MINB>
 __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const float* __restrict__ in,
@@ -79,40 +58,42 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     // input (kh, kw, c) sits at base + offset when its row and column are inside the map
     const long long base = ((img * p.H_in + (h_out - p.pad)) * p.W_in + (w_out - p.pad)) * p.C_in;
 
-    int key[TKEYS];
+    // the pixel's events as keys, inserted in order into the thread's own
+    // shared-memory column (keys are distinct: the input index is part of
+    // each; inputs come in index order, so a key of an already seen step
+    // lands at the end at once)
+    int* col = s_keys + threadIdx.x;                         // entry e at col[e * TW * 32]
     int n_ev = 0;
-#pragma unroll
-    for (int f = 0; f < TKEYS; ++f) {
-        key[f] = KEY_NONE;
-        if (f < fan) {
-            const int4 tp = s_tap[f];
-            if ((unsigned)(h_out + tp.x) < (unsigned)p.H_in && (unsigned)(w_out + tp.y) < (unsigned)p.W_in) {
-                const float t = __ldg(in + (base + tp.z));
-                if (t < p.inf_time) {
-                    int b = (int)floorf(t - p.tfs);
-                    if (b < 0) b = 0;
-                    if (b < p.T) {
-                        int ti;
-                        if (p.lut_mode == VDT_LUT_BY_TB) {
-                            ti = b;
-                        } else {
-                            ti = (int)t;
-                            ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
-                        }
-                        key[f] = (b << 18) | (f << 13) | ti;
-                        ++n_ev;
+#pragma unroll 4
+    for (int f = 0; f < fan; ++f) {
+        const int4 tp = s_tap[f];
+        if ((unsigned)(h_out + tp.x) < (unsigned)p.H_in && (unsigned)(w_out + tp.y) < (unsigned)p.W_in) {
+            const float t = __ldg(in + (base + tp.z));
+            if (t < p.inf_time) {
+                int b = (int)floorf(t - p.tfs);
+                if (b < 0) b = 0;
+                if (b < p.T) {
+                    int ti;
+                    if (p.lut_mode == VDT_LUT_BY_TB) {
+                        ti = b;
+                    } else {
+                        ti = (int)t;
+                        ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
                     }
+                    const int key = (b << 18) | (f << 13) | ti;
+                    int pos = n_ev;
+                    while (pos > 0) {
+                        const int prev = col[(pos - 1) * (TW * 32)];
+                        if (prev < key) break;
+                        col[pos * (TW * 32)] = prev;
+                        --pos;
+                    }
+                    col[pos * (TW * 32)] = key;
+                    ++n_ev;
                 }
             }
         }
     }
-
-    // sorted once (keys are distinct: the input index is part of each), the
-    // events first; staged in the thread's own shared-memory column
-    sort_keys<TKEYS>(key);
-#pragma unroll
-    for (int e = 0; e < TKEYS; ++e)
-        if (e < n_ev) s_keys[e * (TW * 32) + threadIdx.x] = key[e];
 
     Lanes<CO> nu;
 #pragma unroll
