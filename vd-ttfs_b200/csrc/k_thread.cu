@@ -22,9 +22,16 @@ namespace {
 constexpr int TW = 4;             // warps per CTA
 constexpr int TKEYS = 32;         // inputs per pixel at most (keys per thread column)
 
-template <int CO, int MINB>
+// POOL: the layer's 2x2 min pool (k_pooling t1:164-181, t2:192-209) fused
+// in: thread t integrates pixel (2 ph + (t & 3) / 2, 2 pw + (t & 1)) of
+// pooled position t / 4, the four lanes of a quad take the minimum of their
+// first-spike times by shuffles and one writes the pooled map p.out
+// [B, H_out / 2, W_out / 2, C_out]; a last odd row or column is not computed
+// (no pooled output reads it).  n_thr counts threads (pixels, or 4 per pooled
+// position).
+template <int CO, int MINB, bool POOL>
 __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const float* __restrict__ in,
-                                                          long long n_pix) {
+                                                          long long n_thr) {
     extern __shared__ __align__(16) float tsm[];
     __shared__ int s_floor, s_mono;
     chain_release();
@@ -49,12 +56,29 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     const ThTables tt = stage_thresholds(p, s_th, s_thx, &s_floor, &s_mono);   // ends with __syncthreads
     chain_wait();                                            // the input map is complete
 
-    const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (pix >= n_pix) return;
-    const int w_out = (int)(pix % p.W_out);
-    const long long r = pix / p.W_out;
-    const int h_out = (int)(r % p.H_out);
-    const long long img = r / p.H_out;
+    const long long thr = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    // a pooled run keeps every thread to the end (the quads' shuffles); others
+    // leave at once past the last pixel
+    if (!POOL && thr >= n_thr) return;
+    const bool valid = thr < n_thr;
+    int w_out, h_out;
+    long long img, pq = 0;
+    if constexpr (POOL) {
+        const int PW = p.W_out / 2, PH = p.H_out / 2;
+        pq = valid ? thr >> 2 : 0;
+        const int sub = (int)(thr & 3);
+        const int pw = (int)(pq % PW);
+        const long long rq = pq / PW;
+        w_out = 2 * pw + (sub & 1);
+        h_out = 2 * (int)(rq % PH) + (sub >> 1);
+        img = rq / PH;
+    } else {
+        w_out = (int)(thr % p.W_out);
+        const long long r = thr / p.W_out;
+        h_out = (int)(r % p.H_out);
+        img = r / p.H_out;
+    }
+    const long long pix = (img * p.H_out + h_out) * p.W_out + w_out;
     // input (kh, kw, c) sits at base + offset when its row and column are inside the map
     const long long base = ((img * p.H_in + (h_out - p.pad)) * p.W_in + (w_out - p.pad)) * p.C_in;
 
@@ -64,8 +88,9 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     // lands at the end at once)
     int* col = s_keys + threadIdx.x;                         // entry e at col[e * TW * 32]
     int n_ev = 0;
+    const int fan_t = valid ? fan : 0;
 #pragma unroll 4
-    for (int f = 0; f < fan; ++f) {
+    for (int f = 0; f < fan_t; ++f) {
         const int4 tp = s_tap[f];
         if ((unsigned)(h_out + tp.x) < (unsigned)p.H_in && (unsigned)(w_out + tp.y) < (unsigned)p.W_in) {
             const float t = __ldg(in + (base + tp.z));
@@ -101,7 +126,7 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         nu.carry[c] = c < p.C_out ? __ldg(p.bias + c) : 0.0f;
         nu.res[c] = p.inf_time;
         nu.acc[c] = 0.0f;
-        nu.alive[c] = c < p.C_out;
+        nu.alive[c] = valid && c < p.C_out;
     }
     int cur = -1, next_t = 0;
     for (int e = 0; e < n_ev && nu.any(); ++e) {
@@ -133,10 +158,26 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         next_t = cur + 1;
     }
     if (nu.any()) nu.close_empty(next_t, p.T, tt);
-    float* o = p.out + pix * p.C_out;
+    if constexpr (POOL) {
 #pragma unroll
-    for (int c = 0; c < CO; ++c)
-        if (c < p.C_out) o[c] = nu.res[c];
+        for (int c = 0; c < CO; ++c) {
+            float m = nu.res[c];
+            m = fminf(m, __shfl_xor_sync(FULL_MASK, m, 1));
+            m = fminf(m, __shfl_xor_sync(FULL_MASK, m, 2));
+            nu.res[c] = fminf(p.inf_time, m);                // k_pooling starts from INF_TIME
+        }
+        if (valid && (thr & 3) == 0) {
+            float* o = p.out + pq * p.C_out;
+#pragma unroll
+            for (int c = 0; c < CO; ++c)
+                if (c < p.C_out) o[c] = nu.res[c];
+        }
+    } else {
+        float* o = p.out + pix * p.C_out;
+#pragma unroll
+        for (int c = 0; c < CO; ++c)
+            if (c < p.C_out) o[c] = nu.res[c];
+    }
 }
 
 size_t thread_smem(int CO, int T, int decay_len) {
@@ -144,15 +185,15 @@ size_t thread_smem(int CO, int T, int decay_len) {
            (size_t)(decay_len + 2 * T) * sizeof(float);
 }
 
-template <int CO>
-cudaError_t launch_thread_c(const IntegParams& p, const float* in, cudaStream_t s, long long n_pix) {
+template <int CO, bool POOL>
+cudaError_t launch_thread_c(const IntegParams& p, const float* in, cudaStream_t s, long long n_thr) {
     const size_t smem = thread_smem(CO, p.T, p.decay_len);
     constexpr int REGS = CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO;   // keys + lane state
     constexpr int MINB = (65536 / (TW * 32 * REGS)) > 8 ? 8 : (65536 / (TW * 32 * REGS));
-    auto kern = k_thread<CO, MINB>;
-    const long long blocks = (n_pix + TW * 32 - 1) / (TW * 32);
+    auto kern = k_thread<CO, MINB, POOL>;
+    const long long blocks = (n_thr + TW * 32 - 1) / (TW * 32);
     if (blocks >= (1ll << 31)) return cudaErrorInvalidValue;
-    return launch_chain(kern, dim3((unsigned)blocks), dim3(TW * 32), smem, s, p, in, n_pix);
+    return launch_chain(kern, dim3((unsigned)blocks), dim3(TW * 32), smem, s, p, in, n_thr);
 }
 
 }  // namespace
@@ -166,8 +207,16 @@ bool thread_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_le
 cudaError_t launch_thread(const IntegParams& p, const float* in, cudaStream_t s) {
     const long long n_pix = (long long)p.B * p.H_out * p.W_out;
     if (n_pix <= 0) return cudaSuccess;
-    if (p.C_out <= 8) return launch_thread_c<8>(p, in, s, n_pix);
-    return launch_thread_c<16>(p, in, s, n_pix);
+    if (p.C_out <= 8) return launch_thread_c<8, false>(p, in, s, n_pix);
+    return launch_thread_c<16, false>(p, in, s, n_pix);
+}
+
+cudaError_t launch_thread_pooled(const IntegParams& p, const float* in, cudaStream_t s) {
+    if (p.H_out < 2 || p.W_out < 2) return cudaErrorInvalidValue;
+    const long long n_thr = 4ll * p.B * (p.H_out / 2) * (p.W_out / 2);
+    if (n_thr <= 0) return cudaSuccess;
+    if (p.C_out <= 8) return launch_thread_c<8, true>(p, in, s, n_thr);
+    return launch_thread_c<16, true>(p, in, s, n_thr);
 }
 
 }  // namespace vdt

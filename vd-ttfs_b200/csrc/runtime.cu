@@ -542,6 +542,7 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
         float* y = (last && !ly.d.pool_after) ? d_out : c->act[ai];
         if (trace && trace[i] && !last) y = trace[i];
         if (trace && trace[i] && last && ly.d.pool_after) y = trace[i];
+        bool pooled = false;                                 // the layer's pool ran fused into it
         if (ly.d.out == VDT_OUT_VMEM) {
             StageTimer st(c, i, 1);
             VDT_CUDA(launch_layer_vmem(x, ly.W, ly.bias, ly.decay, B, ly.C_in, ly.C_out, cfg.T,
@@ -591,10 +592,24 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
                 VDT_CUDA(launch_bucketize(bp, s));
             }
             StageTimer st(c, i, 1);
-            if (kern == VDT_KERNEL_THREAD && !fe) VDT_CUDA(launch_thread(ip, x, s));
-            else if (dense) VDT_CUDA(launch_dense(ip, x, s));
+            if (kern == VDT_KERNEL_THREAD && !fe) {
+                // k_thread writes the pooled map itself when nobody asks for
+                // the layer's own map (not traced)
+                if (ly.d.pool_after && !(trace && trace[i]) && ly.H_out >= 2 && ly.W_out >= 2) {
+                    if (last) ip.out = d_out;
+                    VDT_CUDA(launch_thread_pooled(ip, x, s));
+                    pooled = true;
+                } else {
+                    VDT_CUDA(launch_thread(ip, x, s));
+                }
+            } else if (dense) VDT_CUDA(launch_dense(ip, x, s));
             else if (kern == VDT_KERNEL_SORTED) VDT_CUDA(launch_sorted(ip, s));
             else VDT_CUDA(launch_integrate(ip, s));
+        }
+        if (pooled) {                                        // y (or d_out) holds the pooled map
+            x = last ? d_out : y;
+            if (!last && y == c->act[ai]) ai = (ai + 1) % 3;
+            continue;
         }
         if (trace && trace[i] && y != trace[i])
             VDT_CUDA(cudaMemcpyAsync(trace[i], y, (size_t)B * ly.H_out * ly.W_out * ly.C_out * sizeof(float),

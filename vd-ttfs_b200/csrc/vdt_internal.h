@@ -103,6 +103,9 @@ cudaError_t launch_dense_culif(const IntegParams& p, const float* in, cudaStream
 // One thread per output pixel for narrow conv layers (K*K*C_in <= 32,
 // C_out <= 16): reads the NHWC spike map directly, same results.
 cudaError_t launch_thread(const IntegParams& p, const float* in, cudaStream_t s);
+// The same with the layer's 2x2 min pool fused in: p.out is the pooled map
+// [B, H_out / 2, W_out / 2, C_out] (H_out, W_out >= 2).
+cudaError_t launch_thread_pooled(const IntegParams& p, const float* in, cudaStream_t s);
 bool thread_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len);
 
 // Chunk integrator with per-chunk slot sorting (reference bucket layout,
