@@ -158,12 +158,13 @@ def layer_bytes(net, events_per_layer, B):
 
 def launches_per_step(net, kernels, pixels=True):
     """Kernel launches of one inference: encode, per layer bucketize (not for
-    k_dense / k_layer_vmem layers) + integrator, pools, readout."""
+    k_dense / k_thread / k_layer_vmem layers) + integrator, pools (a k_thread
+    layer's pool is fused into it), readout."""
     from vdttfs.engine import KERNEL_DENSE, KERNEL_THREAD, KERNEL_VMEM
     n = 1 if pixels else 0
     for l, k in zip(net.layers, kernels):
         n += 1 if k in (KERNEL_DENSE, KERNEL_THREAD, KERNEL_VMEM) else 2
-        n += 1 if l.pool_after else 0
+        n += 1 if l.pool_after and k != KERNEL_THREAD else 0
     return n + 1        # readout
 
 

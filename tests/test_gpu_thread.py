@@ -41,7 +41,20 @@ def _narrow_nets():
         (c(1, 5, 5, nets.PAD_VALID), c(5, 16, 2, nets.PAD_VALID, True), f(16 * 7 * 6, 10)),
         T=37, delta=8, tfs=0.0, lut_mode=nets.LUT_BY_TB, decay_len=37,
         readout=nets.READ_ARGMIN_FIRST, tc_in=17.452274, encoder=nets.ENC_LINEAR)
-    return {"narrow_vgg": vgg_like, "narrow_lenet": lenet_like}
+    # 33 to 255 inputs per pixel (k_thread's per-thread counting sort):
+    # task-1 semantics with a 150-input pooled layer, task-2 semantics with
+    # 252 inputs (28 channels x 3x3)
+    wide_lenet = nets.NetSpec(
+        "wide_lenet", 14, 13, 6,
+        (c(6, 16, 5, nets.PAD_VALID, True), c(16, 7, 3, nets.PAD_SAME), f(5 * 4 * 7, 10)),
+        T=80, delta=16, tfs=0.0, lut_mode=nets.LUT_BY_TB, decay_len=80,
+        readout=nets.READ_ARGMIN_FIRST, tc_in=17.452274, encoder=nets.ENC_LINEAR)
+    wide_vgg = nets.NetSpec(
+        "wide_vgg", 7, 6, 28,
+        (c(28, 12, 3, nets.PAD_SAME, True), c(12, 16, 3, nets.PAD_SAME), f(3 * 3 * 16, 10, nets.OUT_VMEM)),
+        T=40, delta=4, tfs=40.0, lut_mode=nets.LUT_BY_TIN, decay_len=41,
+        readout=nets.READ_ARGMAX, tc_in=34.75016403198242, encoder=nets.ENC_LINEAR)
+    return {"narrow_vgg": vgg_like, "narrow_lenet": lenet_like, "wide_lenet": wide_lenet, "wide_vgg": wide_vgg}
 
 
 def _case(name, B, td=0.0, gains=None):
@@ -54,7 +67,9 @@ def _case(name, B, td=0.0, gains=None):
 
 CASES = [("lenet5", 64, 0.0, None), ("lenet_ref", 32, 0.0, None),
          ("narrow_vgg", 6, 0.0, [1.5, 1.5, 2.0, 1.0]), ("narrow_vgg", 5, 3.0, [1.5, 1.5, 2.0, 1.0]),
-         ("narrow_lenet", 7, 0.0, [0.8, 1.2, 1.0]), ("narrow_lenet", 3, 2.0, [0.8, 1.2, 1.0])]
+         ("narrow_lenet", 7, 0.0, [0.8, 1.2, 1.0]), ("narrow_lenet", 3, 2.0, [0.8, 1.2, 1.0]),
+         ("wide_lenet", 5, 0.0, [1.0, 1.2, 1.0]), ("wide_lenet", 4, 3.0, [1.0, 1.2, 1.0]),
+         ("wide_vgg", 4, 0.0, [1.0, 1.2, 1.0]), ("wide_vgg", 3, 2.0, [1.0, 1.2, 1.0])]
 
 
 @pytest.mark.parametrize("name,B,td,gains", CASES, ids=[f"{c[0]}-B{c[1]}-td{c[2]}" for c in CASES])
@@ -68,6 +83,8 @@ def test_thread_integrator_bitexact(O, dev, name, B, td, gains):
     kinds = ctx.layer_kernels()
     thread_layers = [i for i, k in enumerate(kinds) if k == E.KERNEL_THREAD]
     assert thread_layers, f"no layer of {name} runs k_thread: {kinds}"
+    if name.startswith("wide"):
+        assert thread_layers[:2] == [0, 1], kinds
 
     def check(tag):
         maps, out, pred = ctx.trace(_t(spikes, dev))
@@ -120,7 +137,8 @@ def test_dense_two_pixels_per_warp_bitexact(O, dev, c_out, B):
     """k_dense with at most 16 output channels runs two pixels per warp
     (k_dense_pair) outside counting passes: odd pixel counts (the last warp
     holds one pixel), 1 to 16 channels, and 17 channels (one pixel per warp)
-    give the oracle's maps bit for bit, with and without counting."""
+    give the oracle's maps bit for bit, with and without counting.  Layers
+    this narrow run k_thread by default, so k_dense is chosen explicitly."""
     from vdttfs import engine as E, nets, synth
     c, f = nets._conv, nets._fc
     net = nets.NetSpec(
@@ -134,7 +152,8 @@ def test_dense_two_pixels_per_warp_bitexact(O, dev, c_out, B):
     assert 0.0 < np.mean(ref["maps"][0] < net.inf_time) < 1.0
     m = E.Model(net, layers, lut_source=E.LUT_HOST_LIBM)
     ctx = E.Context(m, B)
-    assert ctx.layer_kernels()[0] == E.KERNEL_DENSE
+    assert ctx.layer_kernels()[0] == (E.KERNEL_THREAD if c_out <= 16 else E.KERNEL_DENSE)
+    ctx.set_layer_kernel(0, E.KERNEL_DENSE)
     for counting in (False, True):
         ctx.set_counting(counting)
         maps, out, pred = ctx.trace(_t(spikes, dev))

@@ -1,5 +1,5 @@
-// k_thread.cu -- integrator for narrow conv layers (K*K*C_in <= 32 inputs per
-// pixel, C_out <= 16): one thread per output pixel, all of its output
+// k_thread.cu -- integrator for narrow conv layers (C_out <= 16, K*K*C_in <=
+// 255 inputs per pixel): one thread per output pixel, all of its output
 // channels.  Same results as k_bucketize + k_conv_bucketed (t1:45-162,
 // t2:45-170), bit for bit.
 //
@@ -29,25 +29,40 @@ constexpr int TKEYS = 32;         // inputs per pixel at most (keys per thread c
 // [B, H_out / 2, W_out / 2, C_out]; a last odd row or column is not computed
 // (no pooled output reads it).  n_thr counts threads (pixels, or 4 per pooled
 // position).
-template <int CO, int MINB, bool POOL>
+//
+// WIDE (33 to 255 inputs per pixel): the events are ordered by a per-thread
+// counting sort instead of insertion.  Pass 1 counts each step's events in
+// byte counters (a shared-memory column per thread), an exclusive scan turns
+// them into starts, pass 2 reads the inputs again (L1) and places each
+// event's input index (and, for LUTs indexed by t_in, its LUT index) in the
+// thread's byte columns; step b's events then sit in input order in
+// [start b, start b+1) -- the reference's chain order.
+template <int CO, int MINB, bool POOL, bool WIDE>
 __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const float* __restrict__ in,
                                                           long long n_thr) {
     extern __shared__ __align__(16) float tsm[];
     __shared__ int s_floor, s_mono;
     chain_release();
+    constexpr int NT = TW * 32;
     const int fan = p.K * p.K * p.C_in;
+    const int NF = WIDE ? fan : TKEYS;                       // weight / tap rows
     // weights padded to CO columns (zeros past C_out), one row per input
-    float* s_w = tsm;                                        // [TKEYS][CO]
-    int4* s_tap = reinterpret_cast<int4*>(s_w + TKEYS * CO); // per input: kh - pad, kw - pad, offset
-    int* s_keys = reinterpret_cast<int*>(s_tap + TKEYS);    // [TKEYS][TW * 32]: a column per thread
-    float* s_decay = reinterpret_cast<float*>(s_keys + TKEYS * TW * 32);
+    float* s_w = tsm;                                        // [NF][CO]
+    int4* s_tap = reinterpret_cast<int4*>(s_w + NF * CO);   // per input: kh - pad, kw - pad, offset
+    float* s_decay = reinterpret_cast<float*>(s_tap + NF);
     float* s_th = s_decay + p.decay_len;
     float* s_thx = s_th + p.T;
-    for (int i = threadIdx.x; i < TKEYS * CO; i += blockDim.x) {
+    // per-thread columns after the tables: narrow, TKEYS int keys; wide, byte
+    // counters [T + 1], event input indices [fan] and LUT indices [fan]
+    int* s_keys = reinterpret_cast<int*>(s_thx + p.T);      // [TKEYS][NT]
+    unsigned char* s_cnt = reinterpret_cast<unsigned char*>(s_thx + p.T);   // [T + 1][NT]
+    unsigned char* s_evf = s_cnt + (p.T + 1) * NT;           // [fan][NT]
+    unsigned char* s_evt = s_evf + fan * NT;                 // [fan][NT] (LUT by t_in only)
+    for (int i = threadIdx.x; i < NF * CO; i += blockDim.x) {
         const int f = i / CO, c = i - f * CO;
         s_w[i] = (f < fan && c < p.C_out) ? p.W[f * p.C_out + c] : 0.0f;
     }
-    for (int f = threadIdx.x; f < TKEYS; f += blockDim.x) {
+    for (int f = threadIdx.x; f < NF; f += blockDim.x) {
         const int tap = f / p.C_in, c = f - tap * p.C_in;
         const int kh = tap / p.K, kw = tap - kh * p.K;
         s_tap[f] = make_int4(kh - p.pad, kw - p.pad, (kh * p.W_in + kw) * p.C_in + c, 0);
@@ -82,39 +97,87 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     // input (kh, kw, c) sits at base + offset when its row and column are inside the map
     const long long base = ((img * p.H_in + (h_out - p.pad)) * p.W_in + (w_out - p.pad)) * p.C_in;
 
-    // the pixel's events as keys, inserted in order into the thread's own
-    // shared-memory column (keys are distinct: the input index is part of
-    // each; inputs come in index order, so a key of an already seen step
-    // lands at the end at once)
-    int* col = s_keys + threadIdx.x;                         // entry e at col[e * TW * 32]
-    int n_ev = 0;
-    const int fan_t = valid ? fan : 0;
-#pragma unroll 4
-    for (int f = 0; f < fan_t; ++f) {
+    // the event of input f, or -1: its step and LUT index
+    auto event_of = [&](int f, int& ti) -> int {
         const int4 tp = s_tap[f];
-        if ((unsigned)(h_out + tp.x) < (unsigned)p.H_in && (unsigned)(w_out + tp.y) < (unsigned)p.W_in) {
-            const float t = __ldg(in + (base + tp.z));
-            if (t < p.inf_time) {
-                int b = (int)floorf(t - p.tfs);
-                if (b < 0) b = 0;
-                if (b < p.T) {
-                    int ti;
-                    if (p.lut_mode == VDT_LUT_BY_TB) {
-                        ti = b;
-                    } else {
-                        ti = (int)t;
-                        ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+        if ((unsigned)(h_out + tp.x) >= (unsigned)p.H_in || (unsigned)(w_out + tp.y) >= (unsigned)p.W_in) return -1;
+        const float t = __ldg(in + (base + tp.z));
+        if (!(t < p.inf_time)) return -1;
+        int b = (int)floorf(t - p.tfs);
+        if (b < 0) b = 0;
+        if (b >= p.T) return -1;
+        if (p.lut_mode == VDT_LUT_BY_TB) {
+            ti = b;
+        } else {
+            ti = (int)t;
+            ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+        }
+        return b;
+    };
+    unsigned char* cnt = s_cnt + threadIdx.x;                // entry b at cnt[b * NT]
+    if constexpr (WIDE) {
+        for (int b = 0; b <= p.T; ++b) cnt[b * NT] = 0;
+        const int fan_t = valid ? fan : 0;
+#pragma unroll 4
+        for (int f = 0; f < fan_t; ++f) {                    // pass 1: counts
+            int ti;
+            const int b = event_of(f, ti);
+            if (b >= 0) cnt[b * NT] = (unsigned char)(cnt[b * NT] + 1);
+        }
+        int run = 0;
+        for (int b = 0; b < p.T; ++b) {                      // exclusive starts
+            const int c = cnt[b * NT];
+            cnt[b * NT] = (unsigned char)run;
+            run += c;
+        }
+#pragma unroll 4
+        for (int f = 0; f < fan_t; ++f) {                    // pass 2: place, input order kept
+            int ti;
+            const int b = event_of(f, ti);
+            if (b >= 0) {
+                const int pos = cnt[b * NT];
+                s_evf[pos * NT + threadIdx.x] = (unsigned char)f;
+                if (p.lut_mode != VDT_LUT_BY_TB) s_evt[pos * NT + threadIdx.x] = (unsigned char)ti;
+                cnt[b * NT] = (unsigned char)(pos + 1);
+            }
+        }
+        // cnt[b] is now the end of step b's events
+    }
+    int n_ev = 0;
+    if constexpr (!WIDE) {
+        // the pixel's events as keys, inserted in order into the thread's own
+        // shared-memory column (keys are distinct: the input index is part of
+        // each; inputs come in index order, so a key of an already seen step
+        // lands at the end at once)
+        int* col = s_keys + threadIdx.x;                         // entry e at col[e * TW * 32]
+        const int fan_t = valid ? fan : 0;
+    #pragma unroll 4
+        for (int f = 0; f < fan_t; ++f) {
+            const int4 tp = s_tap[f];
+            if ((unsigned)(h_out + tp.x) < (unsigned)p.H_in && (unsigned)(w_out + tp.y) < (unsigned)p.W_in) {
+                const float t = __ldg(in + (base + tp.z));
+                if (t < p.inf_time) {
+                    int b = (int)floorf(t - p.tfs);
+                    if (b < 0) b = 0;
+                    if (b < p.T) {
+                        int ti;
+                        if (p.lut_mode == VDT_LUT_BY_TB) {
+                            ti = b;
+                        } else {
+                            ti = (int)t;
+                            ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+                        }
+                        const int key = (b << 18) | (f << 13) | ti;
+                        int pos = n_ev;
+                        while (pos > 0) {
+                            const int prev = col[(pos - 1) * (TW * 32)];
+                            if (prev < key) break;
+                            col[pos * (TW * 32)] = prev;
+                            --pos;
+                        }
+                        col[pos * (TW * 32)] = key;
+                        ++n_ev;
                     }
-                    const int key = (b << 18) | (f << 13) | ti;
-                    int pos = n_ev;
-                    while (pos > 0) {
-                        const int prev = col[(pos - 1) * (TW * 32)];
-                        if (prev < key) break;
-                        col[pos * (TW * 32)] = prev;
-                        --pos;
-                    }
-                    col[pos * (TW * 32)] = key;
-                    ++n_ev;
                 }
             }
         }
@@ -128,36 +191,63 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         nu.acc[c] = 0.0f;
         nu.alive[c] = valid && c < p.C_out;
     }
-    int cur = -1, next_t = 0;
-    for (int e = 0; e < n_ev && nu.any(); ++e) {
-        const int m = s_keys[e * (TW * 32) + threadIdx.x];
-        const int tb = m >> 18;
-        if (tb != cur) {
-            if (cur >= 0) {
-                nu.close_empty(next_t, cur, tt);
-                nu.close_step_bf(cur, tt);
-                next_t = cur + 1;
+    if constexpr (WIDE) {
+        int k = 0, next_t = 0;
+        for (int b = 0; b < p.T && nu.any(); ++b) {
+            const int end = cnt[b * NT];
+            if (end == k) continue;
+            nu.close_empty(next_t, b, tt);
+            for (; k < end; ++k) {
+                const int f = s_evf[k * NT + threadIdx.x];
+                const int ti = p.lut_mode == VDT_LUT_BY_TB ? b : s_evt[k * NT + threadIdx.x];
+                const float lv = s_decay[ti];
+                const float4* wr = reinterpret_cast<const float4*>(s_w + f * CO);
+#pragma unroll
+                for (int q = 0; q < CO / 4; ++q) {
+                    const float4 w4 = wr[q];
+                    const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+                    float a4[4] = {nu.acc[4 * q], nu.acc[4 * q + 1], nu.acc[4 * q + 2], nu.acc[4 * q + 3]};
+                    fma_lanes<4>(a4, w, lv);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) nu.acc[4 * q + j] = a4[j];
+                }
             }
-            cur = tb;
+            nu.close_step_bf(b, tt);
+            next_t = b + 1;
         }
-        const float lv = s_decay[m & 0x1fff];
-        const float4* wr = reinterpret_cast<const float4*>(s_w + ((m >> 13) & 31) * CO);
+        if (nu.any()) nu.close_empty(next_t, p.T, tt);
+    } else {
+        int cur = -1, next_t = 0;
+        for (int e = 0; e < n_ev && nu.any(); ++e) {
+            const int m = s_keys[e * (TW * 32) + threadIdx.x];
+            const int tb = m >> 18;
+            if (tb != cur) {
+                if (cur >= 0) {
+                    nu.close_empty(next_t, cur, tt);
+                    nu.close_step_bf(cur, tt);
+                    next_t = cur + 1;
+                }
+                cur = tb;
+            }
+            const float lv = s_decay[m & 0x1fff];
+            const float4* wr = reinterpret_cast<const float4*>(s_w + ((m >> 13) & 31) * CO);
 #pragma unroll
-        for (int q = 0; q < CO / 4; ++q) {
-            const float4 w4 = wr[q];
-            const float w[4] = {w4.x, w4.y, w4.z, w4.w};
-            float a[4] = {nu.acc[4 * q], nu.acc[4 * q + 1], nu.acc[4 * q + 2], nu.acc[4 * q + 3]};
-            fma_lanes<4>(a, w, lv);
+            for (int q = 0; q < CO / 4; ++q) {
+                const float4 w4 = wr[q];
+                const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+                float a[4] = {nu.acc[4 * q], nu.acc[4 * q + 1], nu.acc[4 * q + 2], nu.acc[4 * q + 3]};
+                fma_lanes<4>(a, w, lv);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) nu.acc[4 * q + j] = a[j];
+                for (int j = 0; j < 4; ++j) nu.acc[4 * q + j] = a[j];
+            }
         }
+        if (cur >= 0 && nu.any()) {
+            nu.close_empty(next_t, cur, tt);
+            nu.close_step_bf(cur, tt);
+            next_t = cur + 1;
+        }
+        if (nu.any()) nu.close_empty(next_t, p.T, tt);
     }
-    if (cur >= 0 && nu.any()) {
-        nu.close_empty(next_t, cur, tt);
-        nu.close_step_bf(cur, tt);
-        next_t = cur + 1;
-    }
-    if (nu.any()) nu.close_empty(next_t, p.T, tt);
     if constexpr (POOL) {
 #pragma unroll
         for (int c = 0; c < CO; ++c) {
@@ -180,43 +270,65 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     }
 }
 
-size_t thread_smem(int CO, int T, int decay_len) {
-    return (size_t)TKEYS * CO * sizeof(float) + TKEYS * sizeof(int4) + (size_t)TKEYS * TW * 32 * sizeof(int) +
-           (size_t)(decay_len + 2 * T) * sizeof(float);
+// shared memory of one CTA: tables, then the per-thread columns
+size_t thread_smem(int CO, int fan, int T, int decay_len, bool wide, bool lut_tin) {
+    const int nf = wide ? fan : TKEYS;
+    size_t b = (size_t)nf * CO * sizeof(float) + (size_t)nf * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
+    if (wide) b += (size_t)TW * 32 * ((T + 1) + fan + (lut_tin ? fan : 0));
+    else b += (size_t)TKEYS * TW * 32 * sizeof(int);
+    return b;
 }
 
-template <int CO, bool POOL>
-cudaError_t launch_thread_c(const IntegParams& p, const float* in, cudaStream_t s, long long n_thr) {
-    const size_t smem = thread_smem(CO, p.T, p.decay_len);
-    constexpr int REGS = CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO;   // keys + lane state
+template <int CO, bool POOL, bool WIDE>
+cudaError_t launch_thread_cw(const IntegParams& p, const float* in, cudaStream_t s, long long n_thr) {
+    const int fan = p.K * p.K * p.C_in;
+    const size_t smem = thread_smem(CO, fan, p.T, p.decay_len, WIDE, p.lut_mode != VDT_LUT_BY_TB);
+    // registers: narrow, the keys' build plus lane state; wide, lane state
+    constexpr int REGS = WIDE ? 4 * CO + 32 : (CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO);
     constexpr int MINB = (65536 / (TW * 32 * REGS)) > 8 ? 8 : (65536 / (TW * 32 * REGS));
-    auto kern = k_thread<CO, MINB, POOL>;
+    auto kern = k_thread<CO, MINB, POOL, WIDE>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
     const long long blocks = (n_thr + TW * 32 - 1) / (TW * 32);
     if (blocks >= (1ll << 31)) return cudaErrorInvalidValue;
     return launch_chain(kern, dim3((unsigned)blocks), dim3(TW * 32), smem, s, p, in, n_thr);
 }
 
+template <bool POOL>
+cudaError_t launch_thread_any(const IntegParams& p, const float* in, cudaStream_t s, long long n_thr) {
+    const bool wide = p.K * p.K * p.C_in > TKEYS;
+    if (p.C_out <= 8) return wide ? launch_thread_cw<8, POOL, true>(p, in, s, n_thr)
+                                  : launch_thread_cw<8, POOL, false>(p, in, s, n_thr);
+    return wide ? launch_thread_cw<16, POOL, true>(p, in, s, n_thr) : launch_thread_cw<16, POOL, false>(p, in, s, n_thr);
+}
+
 }  // namespace
 
 bool thread_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len) {
-    if (is_fc || K * K * C_in > TKEYS || C_out > 16) return false;
-    if (T >= (1 << 13)) return false;                          // 13-bit step / LUT index in the key
-    return thread_smem(16, T, decay_len) <= 48 * 1024;
+    if (is_fc || C_out > 16) return false;
+    const int fan = K * K * C_in;
+    if (fan <= TKEYS) {
+        if (T >= (1 << 13)) return false;                      // 13-bit step / LUT index in the key
+        return thread_smem(16, fan, T, decay_len, false, true) <= 48 * 1024;
+    }
+    // wide: byte counters, input and LUT indices (255 at most each)
+    if (fan > 255 || T > 255 || decay_len > 256) return false;
+    return thread_smem(16, fan, T, decay_len, true, true) <= 100 * 1024;
 }
 
 cudaError_t launch_thread(const IntegParams& p, const float* in, cudaStream_t s) {
     const long long n_pix = (long long)p.B * p.H_out * p.W_out;
     if (n_pix <= 0) return cudaSuccess;
-    if (p.C_out <= 8) return launch_thread_c<8, false>(p, in, s, n_pix);
-    return launch_thread_c<16, false>(p, in, s, n_pix);
+    return launch_thread_any<false>(p, in, s, n_pix);
 }
 
 cudaError_t launch_thread_pooled(const IntegParams& p, const float* in, cudaStream_t s) {
     if (p.H_out < 2 || p.W_out < 2) return cudaErrorInvalidValue;
     const long long n_thr = 4ll * p.B * (p.H_out / 2) * (p.W_out / 2);
     if (n_thr <= 0) return cudaSuccess;
-    if (p.C_out <= 8) return launch_thread_c<8, true>(p, in, s, n_thr);
-    return launch_thread_c<16, true>(p, in, s, n_thr);
+    return launch_thread_any<true>(p, in, s, n_thr);
 }
 
 }  // namespace vdt
