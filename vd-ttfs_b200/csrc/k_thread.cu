@@ -21,6 +21,23 @@ namespace {
 
 constexpr int TW = 4;             // warps per CTA
 constexpr int TKEYS = 32;         // inputs per pixel at most (keys per thread column)
+constexpr int NT = TW * 32;
+
+// weight row stride: CO + 4 floats, so that the rows of a quarter-warp's
+// different inputs start in different 4-bank groups (a CO-float row would put
+// them all in one or two)
+template <int CO> __host__ __device__ constexpr int row_stride() { return CO + 4; }
+
+// a thread's byte column in shared memory, word-interleaved across the CTA:
+// byte k of thread t at ((k / 4) * NT + t) * 4 + k % 4, so every lane of a
+// warp reads its own bank whatever entry it wants
+struct ByteCol {
+    unsigned char* base;                                     // column start of the CTA
+    __device__ __forceinline__ unsigned char& operator[](int k) const {
+        return base[(((k >> 2) * NT + (int)threadIdx.x) << 2) + (k & 3)];
+    }
+};
+__host__ __device__ constexpr size_t col_bytes(int n) { return (size_t)((n + 3) / 4) * NT * 4; }
 
 // POOL: the layer's 2x2 min pool (k_pooling t1:164-181, t2:192-209) fused
 // in: thread t integrates pixel (2 ph + (t & 3) / 2, 2 pw + (t & 1)) of
@@ -43,23 +60,24 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     extern __shared__ __align__(16) float tsm[];
     __shared__ int s_floor, s_mono;
     chain_release();
-    constexpr int NT = TW * 32;
+    constexpr int SW = row_stride<CO>();
     const int fan = p.K * p.K * p.C_in;
     const int NF = WIDE ? fan : TKEYS;                       // weight / tap rows
     // weights padded to CO columns (zeros past C_out), one row per input
-    float* s_w = tsm;                                        // [NF][CO]
-    int4* s_tap = reinterpret_cast<int4*>(s_w + NF * CO);   // per input: kh - pad, kw - pad, offset
+    float* s_w = tsm;                                        // [NF][SW]
+    int4* s_tap = reinterpret_cast<int4*>(s_w + NF * SW);   // per input: kh - pad, kw - pad, offset
     float* s_decay = reinterpret_cast<float*>(s_tap + NF);
     float* s_th = s_decay + p.decay_len;
     float* s_thx = s_th + p.T;
     // per-thread columns after the tables: narrow, TKEYS int keys; wide, byte
-    // counters [T + 1], event input indices [fan] and LUT indices [fan]
+    // counters [T + 1], event input indices [fan] and LUT indices [fan], each
+    // byte column word-interleaved (ByteCol)
     int* s_keys = reinterpret_cast<int*>(s_thx + p.T);      // [TKEYS][NT]
-    unsigned char* s_cnt = reinterpret_cast<unsigned char*>(s_thx + p.T);   // [T + 1][NT]
-    unsigned char* s_evf = s_cnt + (p.T + 1) * NT;           // [fan][NT]
-    unsigned char* s_evt = s_evf + fan * NT;                 // [fan][NT] (LUT by t_in only)
-    for (int i = threadIdx.x; i < NF * CO; i += blockDim.x) {
-        const int f = i / CO, c = i - f * CO;
+    unsigned char* s_cnt = reinterpret_cast<unsigned char*>(s_thx + p.T);
+    unsigned char* s_evf = s_cnt + col_bytes(p.T + 1);
+    unsigned char* s_evt = s_evf + col_bytes(fan);          // LUT by t_in only
+    for (int i = threadIdx.x; i < NF * SW; i += blockDim.x) {
+        const int f = i / SW, c = i - f * SW;
         s_w[i] = (f < fan && c < p.C_out) ? p.W[f * p.C_out + c] : 0.0f;
     }
     for (int f = threadIdx.x; f < NF; f += blockDim.x) {
@@ -114,20 +132,20 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         }
         return b;
     };
-    unsigned char* cnt = s_cnt + threadIdx.x;                // entry b at cnt[b * NT]
+    const ByteCol cnt{s_cnt}, evf{s_evf}, evt{s_evt};
     if constexpr (WIDE) {
-        for (int b = 0; b <= p.T; ++b) cnt[b * NT] = 0;
+        for (int b = 0; b <= p.T; ++b) cnt[b] = 0;
         const int fan_t = valid ? fan : 0;
 #pragma unroll 4
         for (int f = 0; f < fan_t; ++f) {                    // pass 1: counts
             int ti;
             const int b = event_of(f, ti);
-            if (b >= 0) cnt[b * NT] = (unsigned char)(cnt[b * NT] + 1);
+            if (b >= 0) cnt[b] = (unsigned char)(cnt[b] + 1);
         }
         int run = 0;
         for (int b = 0; b < p.T; ++b) {                      // exclusive starts
-            const int c = cnt[b * NT];
-            cnt[b * NT] = (unsigned char)run;
+            const int c = cnt[b];
+            cnt[b] = (unsigned char)run;
             run += c;
         }
 #pragma unroll 4
@@ -135,10 +153,10 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
             int ti;
             const int b = event_of(f, ti);
             if (b >= 0) {
-                const int pos = cnt[b * NT];
-                s_evf[pos * NT + threadIdx.x] = (unsigned char)f;
-                if (p.lut_mode != VDT_LUT_BY_TB) s_evt[pos * NT + threadIdx.x] = (unsigned char)ti;
-                cnt[b * NT] = (unsigned char)(pos + 1);
+                const int pos = cnt[b];
+                evf[pos] = (unsigned char)f;
+                if (p.lut_mode != VDT_LUT_BY_TB) evt[pos] = (unsigned char)ti;
+                cnt[b] = (unsigned char)(pos + 1);
             }
         }
         // cnt[b] is now the end of step b's events
@@ -194,14 +212,14 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     if constexpr (WIDE) {
         int k = 0, next_t = 0;
         for (int b = 0; b < p.T && nu.any(); ++b) {
-            const int end = cnt[b * NT];
+            const int end = cnt[b];
             if (end == k) continue;
             nu.close_empty(next_t, b, tt);
             for (; k < end; ++k) {
-                const int f = s_evf[k * NT + threadIdx.x];
-                const int ti = p.lut_mode == VDT_LUT_BY_TB ? b : s_evt[k * NT + threadIdx.x];
+                const int f = evf[k];
+                const int ti = p.lut_mode == VDT_LUT_BY_TB ? b : evt[k];
                 const float lv = s_decay[ti];
-                const float4* wr = reinterpret_cast<const float4*>(s_w + f * CO);
+                const float4* wr = reinterpret_cast<const float4*>(s_w + f * SW);
 #pragma unroll
                 for (int q = 0; q < CO / 4; ++q) {
                     const float4 w4 = wr[q];
@@ -230,7 +248,7 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
                 cur = tb;
             }
             const float lv = s_decay[m & 0x1fff];
-            const float4* wr = reinterpret_cast<const float4*>(s_w + ((m >> 13) & 31) * CO);
+            const float4* wr = reinterpret_cast<const float4*>(s_w + ((m >> 13) & 31) * SW);
 #pragma unroll
             for (int q = 0; q < CO / 4; ++q) {
                 const float4 w4 = wr[q];
@@ -273,9 +291,9 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
 // shared memory of one CTA: tables, then the per-thread columns
 size_t thread_smem(int CO, int fan, int T, int decay_len, bool wide, bool lut_tin) {
     const int nf = wide ? fan : TKEYS;
-    size_t b = (size_t)nf * CO * sizeof(float) + (size_t)nf * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
-    if (wide) b += (size_t)TW * 32 * ((T + 1) + fan + (lut_tin ? fan : 0));
-    else b += (size_t)TKEYS * TW * 32 * sizeof(int);
+    size_t b = (size_t)nf * (CO + 4) * sizeof(float) + (size_t)nf * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
+    if (wide) b += col_bytes(T + 1) + col_bytes(fan) + (lut_tin ? col_bytes(fan) : 0);
+    else b += (size_t)TKEYS * NT * sizeof(int);
     return b;
 }
 
@@ -283,8 +301,10 @@ template <int CO, bool POOL, bool WIDE>
 cudaError_t launch_thread_cw(const IntegParams& p, const float* in, cudaStream_t s, long long n_thr) {
     const int fan = p.K * p.K * p.C_in;
     const size_t smem = thread_smem(CO, fan, p.T, p.decay_len, WIDE, p.lut_mode != VDT_LUT_BY_TB);
-    // registers: narrow, the keys' build plus lane state; wide, lane state
-    constexpr int REGS = WIDE ? 4 * CO + 32 : (CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO);
+    // registers: narrow, the keys' build plus lane state; wide, 8 per output
+    // channel (a CO = 16 layer's 4 CTAs per SM also fit its shared memory,
+    // and 96 registers spilled)
+    constexpr int REGS = WIDE ? 8 * CO : (CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO);
     constexpr int MINB = (65536 / (TW * 32 * REGS)) > 8 ? 8 : (65536 / (TW * 32 * REGS));
     auto kern = k_thread<CO, MINB, POOL, WIDE>;
     if (smem > 48 * 1024) {
