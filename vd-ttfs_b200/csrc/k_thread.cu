@@ -23,10 +23,47 @@ constexpr int TW = 4;             // warps per CTA
 constexpr int TKEYS = 32;         // inputs per pixel at most (keys per thread column)
 constexpr int NT = TW * 32;
 
-// weight row stride: CO + 4 floats, so that the rows of a quarter-warp's
-// different inputs start in different 4-bank groups (a CO-float row would put
-// them all in one or two)
-template <int CO> __host__ __device__ constexpr int row_stride() { return CO + 4; }
+// weight row stride in floats: past CO, to the next multiple of the vector
+// width (4, or 2 when CO is not a multiple of 4) that is an odd number of
+// vectors, so that the rows of different inputs read by one phase of a
+// vector load start in different bank groups (a CO-float row would put them
+// in one or two)
+__host__ __device__ constexpr int row_stride(int CO) {
+    return CO % 4 == 0 ? ((CO / 4) % 2 == 0 ? CO + 4 : CO + 8) : ((CO / 2) % 2 == 0 ? CO + 2 : CO + 4);
+}
+
+// floats of a weight table of n rows, rounded up to a multiple of 4 (the
+// int4 table after it stays 16-byte aligned)
+__host__ __device__ constexpr int w_floats(int n, int sw) { return (n * sw + 3) & ~3; }
+
+// acc[c] = fma(w[f][c], lv, acc[c]) for the CO channels of weight row f
+template <int CO, int SW>
+__device__ __forceinline__ void add_row(Lanes<CO>& nu, const float* s_w, int f, float lv) {
+    static_assert(CO % 2 == 0 && SW % (CO % 4 == 0 ? 4 : 2) == 0, "row vectors");
+    if constexpr (CO % 4 == 0) {
+        const float4* wr = reinterpret_cast<const float4*>(s_w + f * SW);
+#pragma unroll
+        for (int q = 0; q < CO / 4; ++q) {
+            const float4 w4 = wr[q];
+            const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+            float a[4] = {nu.acc[4 * q], nu.acc[4 * q + 1], nu.acc[4 * q + 2], nu.acc[4 * q + 3]};
+            fma_lanes<4>(a, w, lv);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) nu.acc[4 * q + j] = a[j];
+        }
+    } else {
+        const float2* wr = reinterpret_cast<const float2*>(s_w + f * SW);
+#pragma unroll
+        for (int q = 0; q < CO / 2; ++q) {
+            const float2 w2 = wr[q];
+            const float w[2] = {w2.x, w2.y};
+            float a[2] = {nu.acc[2 * q], nu.acc[2 * q + 1]};
+            fma_lanes<2>(a, w, lv);
+            nu.acc[2 * q] = a[0];
+            nu.acc[2 * q + 1] = a[1];
+        }
+    }
+}
 
 // a thread's byte column in shared memory, word-interleaved across the CTA:
 // byte k of thread t at ((k / 4) * NT + t) * 4 + k % 4, so every lane of a
@@ -60,12 +97,14 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     extern __shared__ __align__(16) float tsm[];
     __shared__ int s_floor, s_mono;
     chain_release();
-    constexpr int SW = row_stride<CO>();
+    constexpr int SW = row_stride(CO);
     const int fan = p.K * p.K * p.C_in;
     const int NF = WIDE ? fan : TKEYS;                       // weight / tap rows
     // weights padded to CO columns (zeros past C_out), one row per input
     float* s_w = tsm;                                        // [NF][SW]
-    int4* s_tap = reinterpret_cast<int4*>(s_w + NF * SW);   // per input: kh - pad, kw - pad, offset
+    // (the weight table rounded up to 16 bytes: SW = 10 with an odd row count
+    // would leave the int4 table misaligned)
+    int4* s_tap = reinterpret_cast<int4*>(s_w + w_floats(NF, SW));   // per input: kh - pad, kw - pad, offset
     float* s_decay = reinterpret_cast<float*>(s_tap + NF);
     float* s_th = s_decay + p.decay_len;
     float* s_thx = s_th + p.T;
@@ -218,17 +257,7 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
             for (; k < end; ++k) {
                 const int f = evf[k];
                 const int ti = p.lut_mode == VDT_LUT_BY_TB ? b : evt[k];
-                const float lv = s_decay[ti];
-                const float4* wr = reinterpret_cast<const float4*>(s_w + f * SW);
-#pragma unroll
-                for (int q = 0; q < CO / 4; ++q) {
-                    const float4 w4 = wr[q];
-                    const float w[4] = {w4.x, w4.y, w4.z, w4.w};
-                    float a4[4] = {nu.acc[4 * q], nu.acc[4 * q + 1], nu.acc[4 * q + 2], nu.acc[4 * q + 3]};
-                    fma_lanes<4>(a4, w, lv);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) nu.acc[4 * q + j] = a4[j];
-                }
+                add_row<CO, SW>(nu, s_w, f, s_decay[ti]);
             }
             nu.close_step_bf(b, tt);
             next_t = b + 1;
@@ -247,17 +276,7 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
                 }
                 cur = tb;
             }
-            const float lv = s_decay[m & 0x1fff];
-            const float4* wr = reinterpret_cast<const float4*>(s_w + ((m >> 13) & 31) * SW);
-#pragma unroll
-            for (int q = 0; q < CO / 4; ++q) {
-                const float4 w4 = wr[q];
-                const float w[4] = {w4.x, w4.y, w4.z, w4.w};
-                float a[4] = {nu.acc[4 * q], nu.acc[4 * q + 1], nu.acc[4 * q + 2], nu.acc[4 * q + 3]};
-                fma_lanes<4>(a, w, lv);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) nu.acc[4 * q + j] = a[j];
-            }
+            add_row<CO, SW>(nu, s_w, (m >> 13) & 31, s_decay[m & 0x1fff]);
         }
         if (cur >= 0 && nu.any()) {
             nu.close_empty(next_t, cur, tt);
@@ -291,7 +310,7 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
 // shared memory of one CTA: tables, then the per-thread columns
 size_t thread_smem(int CO, int fan, int T, int decay_len, bool wide, bool lut_tin) {
     const int nf = wide ? fan : TKEYS;
-    size_t b = (size_t)nf * (CO + 4) * sizeof(float) + (size_t)nf * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
+    size_t b = (size_t)w_floats(nf, row_stride(CO)) * sizeof(float) + (size_t)nf * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
     if (wide) b += col_bytes(T + 1) + col_bytes(fan) + (lut_tin ? col_bytes(fan) : 0);
     else b += (size_t)TKEYS * NT * sizeof(int);
     return b;
@@ -318,10 +337,17 @@ cudaError_t launch_thread_cw(const IntegParams& p, const float* in, cudaStream_t
 
 template <bool POOL>
 cudaError_t launch_thread_any(const IntegParams& p, const float* in, cudaStream_t s, long long n_thr) {
-    const bool wide = p.K * p.K * p.C_in > TKEYS;
-    if (p.C_out <= 8) return wide ? launch_thread_cw<8, POOL, true>(p, in, s, n_thr)
-                                  : launch_thread_cw<8, POOL, false>(p, in, s, n_thr);
-    return wide ? launch_thread_cw<16, POOL, true>(p, in, s, n_thr) : launch_thread_cw<16, POOL, false>(p, in, s, n_thr);
+    // channel lanes: 6, 8, 12 or 16 (the layer's C_out rounded up)
+    if (p.K * p.K * p.C_in > TKEYS) {
+        if (p.C_out <= 6) return launch_thread_cw<6, POOL, true>(p, in, s, n_thr);
+        if (p.C_out <= 8) return launch_thread_cw<8, POOL, true>(p, in, s, n_thr);
+        if (p.C_out <= 12) return launch_thread_cw<12, POOL, true>(p, in, s, n_thr);
+        return launch_thread_cw<16, POOL, true>(p, in, s, n_thr);
+    }
+    if (p.C_out <= 6) return launch_thread_cw<6, POOL, false>(p, in, s, n_thr);
+    if (p.C_out <= 8) return launch_thread_cw<8, POOL, false>(p, in, s, n_thr);
+    if (p.C_out <= 12) return launch_thread_cw<12, POOL, false>(p, in, s, n_thr);
+    return launch_thread_cw<16, POOL, false>(p, in, s, n_thr);
 }
 
 }  // namespace
