@@ -152,7 +152,9 @@ enum {
     VDT_KERNEL_DENSE = 2,   /* k_dense: bucketing fused, reads the spike map */
     VDT_KERNEL_VMEM = 3,    /* k_layer_vmem membrane readout */
     VDT_KERNEL_THREAD = 4   /* k_thread: one thread per output pixel, bucketing
-                               fused; conv layers with K*K*C_in <= 32, C_out <= 16 */
+                               fused; conv layers with C_out <= 16 and K*K*C_in
+                               <= 32 (T < 8192), or 33..255 inputs with T <= 255
+                               and decay_len <= 256 */
 };
 int vdt_ctx_layer_kernels(const vdt_ctx* c, int n_layers, int* kernels);
 /* Force the integrator of one layer (-1 = automatic choice); results are the
