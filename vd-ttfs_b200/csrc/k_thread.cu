@@ -202,41 +202,30 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     }
     int n_ev = 0;
     if constexpr (!WIDE) {
-        // the pixel's events as keys, inserted in order into the thread's own
-        // shared-memory column (keys are distinct: the input index is part of
-        // each; inputs come in index order, so a key of an already seen step
-        // lands at the end at once)
-        int* col = s_keys + threadIdx.x;                         // entry e at col[e * TW * 32]
+        // the pixel's events as keys in the thread's own shared-memory column:
+        // appended without a branch in input order (a non-event's key lands
+        // past the last event and is overwritten or ignored), then sorted by
+        // insertion over the events only (keys are distinct: the input index
+        // is part of each; a step's keys are already in input order)
+        int* col = s_keys + threadIdx.x;                     // entry e at col[e * NT]
         const int fan_t = valid ? fan : 0;
-    #pragma unroll 4
-        for (int f = 0; f < fan_t; ++f) {
-            const int4 tp = s_tap[f];
-            if ((unsigned)(h_out + tp.x) < (unsigned)p.H_in && (unsigned)(w_out + tp.y) < (unsigned)p.W_in) {
-                const float t = __ldg(in + (base + tp.z));
-                if (t < p.inf_time) {
-                    int b = (int)floorf(t - p.tfs);
-                    if (b < 0) b = 0;
-                    if (b < p.T) {
-                        int ti;
-                        if (p.lut_mode == VDT_LUT_BY_TB) {
-                            ti = b;
-                        } else {
-                            ti = (int)t;
-                            ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
-                        }
-                        const int key = (b << 18) | (f << 13) | ti;
-                        int pos = n_ev;
-                        while (pos > 0) {
-                            const int prev = col[(pos - 1) * (TW * 32)];
-                            if (prev < key) break;
-                            col[pos * (TW * 32)] = prev;
-                            --pos;
-                        }
-                        col[pos * (TW * 32)] = key;
-                        ++n_ev;
-                    }
-                }
+#pragma unroll 4
+        for (int f = 0; f < fan_t; ++f) {                    // n_ev <= f < fan <= TKEYS
+            int ti = 0;
+            const int b = event_of(f, ti);
+            col[n_ev * NT] = (int)(((unsigned)b << 18) | (unsigned)(f << 13) | (unsigned)ti);
+            n_ev += b >= 0 ? 1 : 0;
+        }
+        for (int e = 1; e < n_ev; ++e) {
+            const int key = col[e * NT];
+            int pos = e;
+            while (pos > 0) {
+                const int prev = col[(pos - 1) * NT];
+                if (prev < key) break;
+                col[pos * NT] = prev;
+                --pos;
             }
+            col[pos * NT] = key;
         }
     }
 
