@@ -22,6 +22,7 @@ namespace {
 constexpr int TW = 4;             // warps per CTA
 constexpr int TKEYS = 32;         // inputs per pixel at most (keys per thread column)
 constexpr int NT = TW * 32;
+constexpr int LIST_END = 0xff;    // wide form: end of a step's event list (inputs 0..254)
 
 // weight row stride in floats: past CO, to the next multiple of the vector
 // width (4, or 2 when CO is not a multiple of 4) that is an odd number of
@@ -84,13 +85,13 @@ __host__ __device__ constexpr size_t col_bytes(int n) { return (size_t)((n + 3) 
 // (no pooled output reads it).  n_thr counts threads (pixels, or 4 per pooled
 // position).
 //
-// WIDE (33 to 255 inputs per pixel): the events are ordered by a per-thread
-// counting sort instead of insertion.  Pass 1 counts each step's events in
-// byte counters (a shared-memory column per thread), an exclusive scan turns
-// them into starts, pass 2 reads the inputs again (L1) and places each
-// event's input index (and, for LUTs indexed by t_in, its LUT index) in the
-// thread's byte columns; step b's events then sit in input order in
-// [start b, start b+1) -- the reference's chain order.
+// WIDE (33 to 255 inputs per pixel): the events are ordered by one list per
+// step instead of sorted keys.  A single pass over the inputs, from the last
+// to the first, pushes each event's input index onto its step's list (byte
+// columns: a head per step, a link per input, and for LUTs indexed by t_in
+// the event's LUT index), so each list runs in input order -- the
+// reference's chain order inside the step; the walk takes the steps in
+// order and follows each list.
 template <int CO, int MINB, bool POOL, bool WIDE>
 __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const float* __restrict__ in,
                                                           long long n_thr) {
@@ -109,12 +110,12 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     float* s_th = s_decay + p.decay_len;
     float* s_thx = s_th + p.T;
     // per-thread columns after the tables: narrow, TKEYS int keys; wide, byte
-    // counters [T + 1], event input indices [fan] and LUT indices [fan], each
-    // byte column word-interleaved (ByteCol)
+    // columns of list heads [T], list links [fan] and LUT indices [fan], each
+    // word-interleaved (ByteCol)
     int* s_keys = reinterpret_cast<int*>(s_thx + p.T);      // [TKEYS][NT]
-    unsigned char* s_cnt = reinterpret_cast<unsigned char*>(s_thx + p.T);
-    unsigned char* s_evf = s_cnt + col_bytes(p.T + 1);
-    unsigned char* s_evt = s_evf + col_bytes(fan);          // LUT by t_in only
+    unsigned char* s_head = reinterpret_cast<unsigned char*>(s_thx + p.T);
+    unsigned char* s_next = s_head + col_bytes(p.T);
+    unsigned char* s_lut = s_next + col_bytes(fan);         // LUT by t_in only
     for (int i = threadIdx.x; i < NF * SW; i += blockDim.x) {
         const int f = i / SW, c = i - f * SW;
         s_w[i] = (f < fan && c < p.C_out) ? p.W[f * p.C_out + c] : 0.0f;
@@ -171,34 +172,21 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         }
         return b;
     };
-    const ByteCol cnt{s_cnt}, evf{s_evf}, evt{s_evt};
+    const ByteCol head{s_head}, next{s_next}, lut{s_lut};
     if constexpr (WIDE) {
-        for (int b = 0; b <= p.T; ++b) cnt[b] = 0;
-        const int fan_t = valid ? fan : 0;
-#pragma unroll 4
-        for (int f = 0; f < fan_t; ++f) {                    // pass 1: counts
-            int ti;
-            const int b = event_of(f, ti);
-            if (b >= 0) cnt[b] = (unsigned char)(cnt[b] + 1);
-        }
-        int run = 0;
-        for (int b = 0; b < p.T; ++b) {                      // exclusive starts
-            const int c = cnt[b];
-            cnt[b] = (unsigned char)run;
-            run += c;
-        }
-#pragma unroll 4
-        for (int f = 0; f < fan_t; ++f) {                    // pass 2: place, input order kept
-            int ti;
+        // one list per step, linked through the input indices; inputs are
+        // pushed from the last to the first, so each list runs in input order
+        unsigned* hw = reinterpret_cast<unsigned*>(s_head) + threadIdx.x;
+        for (int w = 0; w < (p.T + 3) / 4; ++w) hw[w * NT] = 0xffffffffu;   // LIST_END
+        for (int f = (valid ? fan : 0) - 1; f >= 0; --f) {
+            int ti = 0;
             const int b = event_of(f, ti);
             if (b >= 0) {
-                const int pos = cnt[b];
-                evf[pos] = (unsigned char)f;
-                if (p.lut_mode != VDT_LUT_BY_TB) evt[pos] = (unsigned char)ti;
-                cnt[b] = (unsigned char)(pos + 1);
+                next[f] = head[b];
+                head[b] = (unsigned char)f;
+                if (p.lut_mode != VDT_LUT_BY_TB) lut[f] = (unsigned char)ti;
             }
         }
-        // cnt[b] is now the end of step b's events
     }
     int n_ev = 0;
     if constexpr (!WIDE) {
@@ -238,16 +226,16 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         nu.alive[c] = valid && c < p.C_out;
     }
     if constexpr (WIDE) {
-        int k = 0, next_t = 0;
+        int next_t = 0;
         for (int b = 0; b < p.T && nu.any(); ++b) {
-            const int end = cnt[b];
-            if (end == k) continue;
+            int f = head[b];
+            if (f == LIST_END) continue;
             nu.close_empty(next_t, b, tt);
-            for (; k < end; ++k) {
-                const int f = evf[k];
-                const int ti = p.lut_mode == VDT_LUT_BY_TB ? b : evt[k];
+            do {
+                const int ti = p.lut_mode == VDT_LUT_BY_TB ? b : lut[f];
                 add_row<CO, SW>(nu, s_w, f, s_decay[ti]);
-            }
+                f = next[f];
+            } while (f != LIST_END);
             nu.close_step_bf(b, tt);
             next_t = b + 1;
         }
@@ -300,7 +288,7 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
 size_t thread_smem(int CO, int fan, int T, int decay_len, bool wide, bool lut_tin) {
     const int nf = wide ? fan : TKEYS;
     size_t b = (size_t)w_floats(nf, row_stride(CO)) * sizeof(float) + (size_t)nf * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
-    if (wide) b += col_bytes(T + 1) + col_bytes(fan) + (lut_tin ? col_bytes(fan) : 0);
+    if (wide) b += col_bytes(T) + col_bytes(fan) + (lut_tin ? col_bytes(fan) : 0);
     else b += (size_t)TKEYS * NT * sizeof(int);
     return b;
 }
