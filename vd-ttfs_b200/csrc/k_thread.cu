@@ -100,13 +100,14 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     chain_release();
     constexpr int SW = row_stride(CO);
     const int fan = p.K * p.K * p.C_in;
-    const int NF = WIDE ? fan : TKEYS;                       // weight / tap rows
+    const int NF = WIDE ? fan : TKEYS;                       // weight rows
+    const int NTAP = WIDE ? p.K * p.K : TKEYS;               // tap rows: per tap (wide), per input
     // weights padded to CO columns (zeros past C_out), one row per input
     float* s_w = tsm;                                        // [NF][SW]
     // (the weight table rounded up to 16 bytes: SW = 10 with an odd row count
     // would leave the int4 table misaligned)
-    int4* s_tap = reinterpret_cast<int4*>(s_w + w_floats(NF, SW));   // per input: kh - pad, kw - pad, offset
-    float* s_decay = reinterpret_cast<float*>(s_tap + NF);
+    int4* s_tap = reinterpret_cast<int4*>(s_w + w_floats(NF, SW));   // kh - pad, kw - pad, offset
+    float* s_decay = reinterpret_cast<float*>(s_tap + NTAP);
     float* s_th = s_decay + p.decay_len;
     float* s_thx = s_th + p.T;
     // per-thread columns after the tables: narrow, TKEYS int keys; wide, byte
@@ -120,8 +121,8 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         const int f = i / SW, c = i - f * SW;
         s_w[i] = (f < fan && c < p.C_out) ? p.W[f * p.C_out + c] : 0.0f;
     }
-    for (int f = threadIdx.x; f < NF; f += blockDim.x) {
-        const int tap = f / p.C_in, c = f - tap * p.C_in;
+    for (int f = threadIdx.x; f < NTAP; f += blockDim.x) {
+        const int tap = WIDE ? f : f / p.C_in, c = WIDE ? 0 : f - tap * p.C_in;
         const int kh = tap / p.K, kw = tap - kh * p.K;
         s_tap[f] = make_int4(kh - p.pad, kw - p.pad, (kh * p.W_in + kw) * p.C_in + c, 0);
     }
@@ -155,11 +156,8 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     // input (kh, kw, c) sits at base + offset when its row and column are inside the map
     const long long base = ((img * p.H_in + (h_out - p.pad)) * p.W_in + (w_out - p.pad)) * p.C_in;
 
-    // the event of input f, or -1: its step and LUT index
-    auto event_of = [&](int f, int& ti) -> int {
-        const int4 tp = s_tap[f];
-        if ((unsigned)(h_out + tp.x) >= (unsigned)p.H_in || (unsigned)(w_out + tp.y) >= (unsigned)p.W_in) return -1;
-        const float t = __ldg(in + (base + tp.z));
+    // the event of the input at spike time t, or -1: its step and LUT index
+    auto event_at = [&](float t, int& ti) -> int {
         if (!(t < p.inf_time)) return -1;
         int b = (int)floorf(t - p.tfs);
         if (b < 0) b = 0;
@@ -172,19 +170,31 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         }
         return b;
     };
+    // the same for input f (per-input tap table)
+    auto event_of = [&](int f, int& ti) -> int {
+        const int4 tp = s_tap[f];
+        if ((unsigned)(h_out + tp.x) >= (unsigned)p.H_in || (unsigned)(w_out + tp.y) >= (unsigned)p.W_in) return -1;
+        return event_at(__ldg(in + (base + tp.z)), ti);
+    };
     const ByteCol head{s_head}, next{s_next}, lut{s_lut};
     if constexpr (WIDE) {
         // one list per step, linked through the input indices; inputs are
         // pushed from the last to the first, so each list runs in input order
         unsigned* hw = reinterpret_cast<unsigned*>(s_head) + threadIdx.x;
         for (int w = 0; w < (p.T + 3) / 4; ++w) hw[w * NT] = 0xffffffffu;   // LIST_END
-        for (int f = (valid ? fan : 0) - 1; f >= 0; --f) {
-            int ti = 0;
-            const int b = event_of(f, ti);
-            if (b >= 0) {
-                next[f] = head[b];
-                head[b] = (unsigned char)f;
-                if (p.lut_mode != VDT_LUT_BY_TB) lut[f] = (unsigned char)ti;
+        for (int tap = (valid ? NTAP : 0) - 1; tap >= 0; --tap) {
+            const int4 tp = s_tap[tap];
+            if ((unsigned)(h_out + tp.x) >= (unsigned)p.H_in || (unsigned)(w_out + tp.y) >= (unsigned)p.W_in) continue;
+            const float* src = in + (base + tp.z);
+            for (int c = p.C_in - 1; c >= 0; --c) {
+                int ti = 0;
+                const int b = event_at(__ldg(src + c), ti);
+                if (b >= 0) {
+                    const int f = tap * p.C_in + c;
+                    next[f] = head[b];
+                    head[b] = (unsigned char)f;
+                    if (p.lut_mode != VDT_LUT_BY_TB) lut[f] = (unsigned char)ti;
+                }
             }
         }
     }
@@ -242,7 +252,7 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         if (nu.any()) nu.close_empty(next_t, p.T, tt);
     } else {
         int cur = -1, next_t = 0;
-        for (int e = 0; e < n_ev && nu.any(); ++e) {
+        for (int e = 0; e < n_ev; ++e) {
             const int m = s_keys[e * (TW * 32) + threadIdx.x];
             const int tb = m >> 18;
             if (tb != cur) {
@@ -250,6 +260,7 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
                     nu.close_empty(next_t, cur, tt);
                     nu.close_step_bf(cur, tt);
                     next_t = cur + 1;
+                    if (!nu.any()) break;                    // (cur stays closed)
                 }
                 cur = tb;
             }
@@ -285,9 +296,9 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
 }
 
 // shared memory of one CTA: tables, then the per-thread columns
-size_t thread_smem(int CO, int fan, int T, int decay_len, bool wide, bool lut_tin) {
-    const int nf = wide ? fan : TKEYS;
-    size_t b = (size_t)w_floats(nf, row_stride(CO)) * sizeof(float) + (size_t)nf * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
+size_t thread_smem(int CO, int K, int fan, int T, int decay_len, bool wide, bool lut_tin) {
+    const int nf = wide ? fan : TKEYS, ntap = wide ? K * K : TKEYS;
+    size_t b = (size_t)w_floats(nf, row_stride(CO)) * sizeof(float) + (size_t)ntap * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
     if (wide) b += col_bytes(T) + col_bytes(fan) + (lut_tin ? col_bytes(fan) : 0);
     else b += (size_t)TKEYS * NT * sizeof(int);
     return b;
@@ -296,11 +307,11 @@ size_t thread_smem(int CO, int fan, int T, int decay_len, bool wide, bool lut_ti
 template <int CO, bool POOL, bool WIDE>
 cudaError_t launch_thread_cw(const IntegParams& p, const float* in, cudaStream_t s, long long n_thr) {
     const int fan = p.K * p.K * p.C_in;
-    const size_t smem = thread_smem(CO, fan, p.T, p.decay_len, WIDE, p.lut_mode != VDT_LUT_BY_TB);
-    // registers: narrow, the keys' build plus lane state; wide, 8 per output
-    // channel (a CO = 16 layer's 4 CTAs per SM also fit its shared memory,
-    // and 96 registers spilled)
-    constexpr int REGS = WIDE ? 8 * CO : (CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO);
+    const size_t smem = thread_smem(CO, p.K, fan, p.T, p.decay_len, WIDE, p.lut_mode != VDT_LUT_BY_TB);
+    // registers: narrow, the keys' build plus lane state; wide, lane state
+    // (96 for 16 channels: 5 CTAs per SM, which a 150-input layer's shared
+    // memory also allows)
+    constexpr int REGS = WIDE ? 4 * CO + 32 : (CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO);
     constexpr int MINB = (65536 / (TW * 32 * REGS)) > 8 ? 8 : (65536 / (TW * 32 * REGS));
     auto kern = k_thread<CO, MINB, POOL, WIDE>;
     if (smem > 48 * 1024) {
@@ -334,11 +345,11 @@ bool thread_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_le
     const int fan = K * K * C_in;
     if (fan <= TKEYS) {
         if (T >= (1 << 13)) return false;                      // 13-bit step / LUT index in the key
-        return thread_smem(16, fan, T, decay_len, false, true) <= 48 * 1024;
+        return thread_smem(16, K, fan, T, decay_len, false, true) <= 48 * 1024;
     }
     // wide: byte counters, input and LUT indices (255 at most each)
     if (fan > 255 || T > 255 || decay_len > 256) return false;
-    return thread_smem(16, fan, T, decay_len, true, true) <= 100 * 1024;
+    return thread_smem(16, K, fan, T, decay_len, true, true) <= 100 * 1024;
 }
 
 cudaError_t launch_thread(const IntegParams& p, const float* in, cudaStream_t s) {
