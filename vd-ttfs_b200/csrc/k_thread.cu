@@ -4,15 +4,17 @@
 // t2:45-170), bit for bit.
 //
 // A warp of 32 pixels replaces 32 warps of k_dense, which for a 6-channel
-// layer would leave 26 of 32 lanes idle.  The thread turns its pixel's events
-// into keys (step << 18 | input index << 13 | LUT index), so increasing key
-// order is the reference's order: by step, and inside a step by (tap,
-// channel) -- each neuron's FMA chain.  Each key is inserted in order into
-// the thread's own shared-memory column as it is made (a pixel has few
-// events; a fully unrolled sorting network was slower, its code overflowing
-// the instruction cache).  The thread then walks its sorted events, adds
-// w[input][c] * LUT to every channel's open step, and closes a step when the
-// next key leaves it (lanes.h closes; input-free steps by bisection).
+// layer would leave 26 of 32 lanes idle.  With at most 32 inputs per pixel
+// the thread turns its pixel's events into keys (step << 18 | input index <<
+// 13 | LUT index), so increasing key order is the reference's order: by
+// step, and inside a step by (tap, channel) -- each neuron's FMA chain.  The
+// keys are appended to the thread's own shared-memory column and sorted by
+// insertion over the events only (a pixel has few events; a fully unrolled
+// sorting network was slower, its code overflowing the instruction cache).
+// The thread then walks its sorted events, adds w[input][c] * LUT to every
+// channel's open step, and closes a step when the next key leaves it
+// (lanes.h closes; input-free steps by bisection).  Wider pixels order their
+// events by per-step lists instead (WIDE below).
 #include "lanes.h"
 #include "vdt_internal.h"
 
