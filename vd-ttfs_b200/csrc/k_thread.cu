@@ -172,10 +172,15 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
         }
         return b;
     };
-    // the same for input f (per-input tap table)
+    // the same for input f (per-input tap table); a pixel whose whole window
+    // lies inside the map (every pixel of a valid convolution) skips the
+    // per-input row and column tests
+    const bool inside = h_out >= p.pad && h_out - p.pad + p.K <= p.H_in && w_out >= p.pad &&
+                        w_out - p.pad + p.K <= p.W_in;
     auto event_of = [&](int f, int& ti) -> int {
         const int4 tp = s_tap[f];
-        if ((unsigned)(h_out + tp.x) >= (unsigned)p.H_in || (unsigned)(w_out + tp.y) >= (unsigned)p.W_in) return -1;
+        if (!inside && ((unsigned)(h_out + tp.x) >= (unsigned)p.H_in || (unsigned)(w_out + tp.y) >= (unsigned)p.W_in))
+            return -1;
         return event_at(__ldg(in + (base + tp.z)), ti);
     };
     const ByteCol head{s_head}, next{s_next}, lut{s_lut};
