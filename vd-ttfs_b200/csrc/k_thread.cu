@@ -112,10 +112,10 @@ __global__ void __launch_bounds__(TW * 32, MINB) k_thread(IntegParams p, const f
     float* s_decay = reinterpret_cast<float*>(s_tap + NTAP);
     float* s_th = s_decay + p.decay_len;
     float* s_thx = s_th + p.T;
-    // per-thread columns after the tables: narrow, TKEYS int keys; wide, byte
+    // per-thread columns after the tables: narrow, fan int keys; wide, byte
     // columns of list heads [T], list links [fan] and LUT indices [fan], each
     // word-interleaved (ByteCol)
-    int* s_keys = reinterpret_cast<int*>(s_thx + p.T);      // [TKEYS][NT]
+    int* s_keys = reinterpret_cast<int*>(s_thx + p.T);      // [fan][NT]
     unsigned char* s_head = reinterpret_cast<unsigned char*>(s_thx + p.T);
     unsigned char* s_next = s_head + col_bytes(p.T);
     unsigned char* s_lut = s_next + col_bytes(fan);         // LUT by t_in only
@@ -307,7 +307,7 @@ size_t thread_smem(int CO, int K, int fan, int T, int decay_len, bool wide, bool
     const int nf = wide ? fan : TKEYS, ntap = wide ? K * K : TKEYS;
     size_t b = (size_t)w_floats(nf, row_stride(CO)) * sizeof(float) + (size_t)ntap * sizeof(int4) + (size_t)(decay_len + 2 * T) * sizeof(float);
     if (wide) b += col_bytes(T) + col_bytes(fan) + (lut_tin ? col_bytes(fan) : 0);
-    else b += (size_t)TKEYS * NT * sizeof(int);
+    else b += (size_t)fan * NT * sizeof(int);                // a key per input at most
     return b;
 }
 
@@ -318,8 +318,10 @@ cudaError_t launch_thread_cw(const IntegParams& p, const float* in, cudaStream_t
     // registers: narrow, the keys' build plus lane state; wide, lane state
     // (96 for 16 channels: 5 CTAs per SM, which a 150-input layer's shared
     // memory also allows)
-    constexpr int REGS = WIDE ? 4 * CO + 32 : (CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO);
-    constexpr int MINB = (65536 / (TW * 32 * REGS)) > 8 ? 8 : (65536 / (TW * 32 * REGS));
+    // (48 for a 6-channel narrow layer: 10 CTAs per SM, which its shared
+    // memory, a key column sized by the fan-in, also allows)
+    constexpr int REGS = WIDE ? 4 * CO + 32 : (CO <= 6 ? 48 : CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO);
+    constexpr int MINB = (65536 / (TW * 32 * REGS)) > 10 ? 10 : (65536 / (TW * 32 * REGS));
     auto kern = k_thread<CO, MINB, POOL, WIDE>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
