@@ -318,10 +318,11 @@ cudaError_t launch_thread_cw(const IntegParams& p, const float* in, cudaStream_t
     // registers: narrow, the keys' build plus lane state; wide, lane state
     // (96 for 16 channels: 5 CTAs per SM, which a 150-input layer's shared
     // memory also allows)
-    // (48 for a 6-channel narrow layer: 10 CTAs per SM, which its shared
-    // memory, a key column sized by the fan-in, also allows)
-    constexpr int REGS = WIDE ? 4 * CO + 32 : (CO <= 6 ? 48 : CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO);
-    constexpr int MINB = (65536 / (TW * 32 * REGS)) > 10 ? 10 : (65536 / (TW * 32 * REGS));
+    // (42 for a 6-channel narrow layer: 12 CTAs per SM, which its shared
+    // memory, a key column sized by the fan-in, also allows; the few spills
+    // cost less than the added warps gain)
+    constexpr int REGS = WIDE ? 4 * CO + 32 : (CO <= 6 ? 42 : CO <= 8 ? TKEYS + 2 * CO + 16 : TKEYS + 4 * CO);
+    constexpr int MINB = (65536 / (TW * 32 * REGS)) > 12 ? 12 : (65536 / (TW * 32 * REGS));
     auto kern = k_thread<CO, MINB, POOL, WIDE>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
