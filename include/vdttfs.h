@@ -119,6 +119,40 @@ int vdt_model_info(const vdt_model* m, int* n_layers, int* n_classes, size_t* we
 /* copy layer `layer`'s tables to host: decay_len and T floats */
 int vdt_model_luts(const vdt_model* m, int layer, float* h_decay, float* h_th);
 
+/* Task-3 (DVS gesture) CuLIF network: the topology and constants the
+   reference's task-3 main hard-codes (t3:18-27 and its stage list :267-284;
+   the reference: 2x32x32 input, T 160, delta 32, channels 64/128/128,
+   k 3, hidden 128, 10 classes, decay exp(-1/5) / exp(-1/60), th 5 / 10). */
+typedef struct {
+    int in_c, H, W;       /* sensor polarities and size; H, W multiples of 4 */
+    int T, delta;         /* T_TOTAL and CHUNK */
+    int c1, c2, c3;       /* conv1 (raw frames), conv2, conv3 output channels */
+    int k;                /* conv kernel size (odd, same padding) */
+    int hidden, classes;  /* recurrent FC1 width (multiple of 32, <= 1024), FC2 outputs */
+    float decay_conv, th_conv, decay_fc, th_fc;
+} vdt_dvs_desc;
+
+/* Replaces the task-3 main's weight read (t3:237-241): `blob` is the flat
+   little-endian float32 array in the order of the reference's
+   dvsgesture_weights_meta.txt -- conv1, conv2, conv3 (OIHW), FC1 recurrent
+   [hidden, hidden], FC1 [hidden, c3*(H/4)*(W/4)], FC2 [classes, hidden] --
+   at the offsets those sizes give (1,288,576 floats for the reference's
+   shapes, FC2 at float 1,287,296); a longer blob is accepted (the reference
+   reads a fixed 1,292,032 floats), a shorter one is VDT_ERR_BLOB.  The returned model is used with
+   vdt_ctx_create and the whole-network calls below: vdt_infer,
+   vdt_infer_host, vdt_infer_host_batches and vdt_infer_trace take frames
+   [batch, in_c, H, W, T] (time innermost, the reference's raw input; the
+   input_is_pixels flag is ignored), write FC2's first-spike times
+   [batch, classes] and the argmin readout with class 0 as the start
+   (t3:295-296), and run each batch as one captured CUDA graph with the
+   ctx's workspace.  vdt_infer_trace's d_layer_out[0..6] receive the seven
+   stage maps (conv1, conv2, pool1, conv3, pool2 NCHW; fc1 [batch, hidden];
+   fc2); profiling times the same seven stages.  Per-layer integrator
+   choice, LUTs, counting and sub-batches do not apply (VDT_ERR_UNSUPPORTED
+   or no effect). */
+int vdt_model_load_dvs_flat(const void* blob, size_t nbytes, const vdt_dvs_desc* desc, int device,
+                            vdt_model** out);
+
 /* ------------------------------------------------------------------------
  * Context: workspace (activations, bucket lists) for batches <= max_batch,
  * bound to one stream.  Replaces the reference's cudaMalloc'd g_bkt_* statics
@@ -133,6 +167,11 @@ int vdt_ctx_set_graphs(vdt_ctx* c, int enable);
    executions, as counted by task2 macs/stat_timesorted_macs.cu:136,155) */
 int vdt_ctx_set_counting(vdt_ctx* c, int enable);
 int vdt_ctx_counters(vdt_ctx* c, unsigned long long* events, unsigned long long* fetched);
+/* The same per layer (n_layers entries each, either array may be NULL): the
+   events kept by the layer's bucketing and the synapses its integrator
+   fetched.  Each read, by either call, returns the counts since the previous
+   read and zeroes them. */
+int vdt_ctx_layer_counters(vdt_ctx* c, int n_layers, unsigned long long* events, unsigned long long* fetched);
 /* 1 = time every stage with CUDA events on the ctx stream (forces the eager,
    non-graph path while on); vdt_ctx_layer_times then returns, per layer, the
    milliseconds accumulated since the last read by its bucketize, integrate
@@ -351,6 +390,18 @@ int vdt_conv_layer_noalloc(const float* d_in, int tb_mode, const float* d_kernel
                            int t_min, int B, int H_in, int W_in, int C_in, int H_out,
                            int W_out, int C_out, int K, int pad, int is_fc,
                            const vdt_time_cfg* cfg, float* d_out, vdt_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Measurement helper (no counterpart in the reference)
+ * ---------------------------------------------------------------------- */
+
+/* Measures, on `device` at its current clocks, the FP32 FMA throughput
+   (FMAs per second over independent packed fma.rn.f32x2 chains on every SM)
+   and the L2-to-SM read bandwidth (bytes per second, 16-byte L2-only loads of
+   a 32 MiB L2-resident buffer): the integrators' two limits, one FMA and one
+   4-byte weight read per fetched synapse.  Allocates and frees 32 MiB; runs
+   on the legacy default stream and synchronises it. */
+int vdt_measure_peaks(int device, double* fma_per_s, double* l2_read_bytes_per_s);
 
 #ifdef __cplusplus
 }

@@ -14,10 +14,11 @@ workloads) and its network's run_batch runs on seeded synthetic images (the
 bench generator, HWC -> CHW as its data_io does), torch on every host core.
 These are different discretisations (a full convolution per time step) from
 the event-driven path, so only their speed is reported.
-Needs the reference tree (this machine only); test infrastructure.  Prints
-one JSON line.
+Needs the reference tree ($VDT_REFERENCE, else a directory `reference`
+beside this repository), so it runs where the reference is checked out, not
+on a GPU box; test infrastructure.  Prints one JSON line.
 
-Usage: python tests/ref_torch_cpu.py [vgg16|lenet_ref] [images]
+Usage: python oracle/ref_torch_cpu.py [vgg16|lenet_ref] [images]
 """
 import json
 import os
@@ -28,7 +29,7 @@ import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
-REF_DIR = os.path.join("/root/reference", "task2_vgg16_cifar10", "spikingjelly")
+REF = os.environ.get("VDT_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference")
 sys.path.insert(0, os.path.join(ROOT, "vd-ttfs_b200"))
 
 
@@ -88,7 +89,7 @@ def main():
     threads = os.cpu_count()
     torch.set_num_threads(threads)
     if which == "vgg16":
-        sys.path.insert(0, REF_DIR)
+        sys.path.insert(0, os.path.join(REF, "task2_vgg16_cifar10", "spikingjelly"))
         import baseline_torch as bt                               # noqa: E402  (the reference's module)
         import weights_io                                         # noqa: E402
         net = nets.vgg16()
@@ -96,7 +97,7 @@ def main():
         img = synth.images(3, n, 32, 32, 3, 0.0)                  # NHWC, the bench's images
         impl, steps = "baseline_torch.py, torch CPU", bt.TIME_STEPS
     else:
-        sys.path.insert(0, os.path.join("/root/reference", "task1_lenet_mnist", "spikingjelly"))
+        sys.path.insert(0, os.path.join(REF, "task1_lenet_mnist", "spikingjelly"))
         spikingjelly_stand_in()
         import baseline_spikingjelly_mnist as bt                  # noqa: E402  (the reference's module)
         import weights_io                                         # noqa: E402

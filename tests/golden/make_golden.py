@@ -18,6 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(ROOT, "vd-ttfs_b200"))
 sys.path.insert(0, os.path.join(ROOT, "tests"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 import torch  # noqa: E402
 
@@ -193,7 +194,9 @@ def gen_task3(out):
 
 
 def main():
-    out = sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "gpurun_out", "golden")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py OUT_DIR")
+    out = sys.argv[1]
     os.makedirs(out, exist_ok=True)
     for task in (1, 2):
         gen_task12(task, out)

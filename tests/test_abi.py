@@ -98,3 +98,32 @@ def test_per_stage_entry_points_reject_bad_arguments():
     assert L.vdt_readout(None, 1, 10, 0, 9999.0, None, None) == 1
     assert L.vdt_pool_min(None, None, 1, 1, 1, 1, 9999.0, None) == 1
     assert L.vdt_infer(None, None, 0, 1, None, None) == 1
+
+
+def test_dvs_flat_blob_validation_happens_before_any_gpu_work():
+    """vdt_model_load_dvs_flat checks the descriptor and the blob's length
+    before it touches a device: the reference-shaped blob holds the layers at
+    the offsets of dvsgesture_weights_meta.txt (FC2 at float 1,287,296)."""
+    from vdttfs import _lib, assets, dvs, nets, synth
+    spec = nets.dvs_ref()
+    layout, total = assets.dvs_flat_layout(spec)
+    assert [off for _, _, off in layout] == [0, 1152, 74880, 222336, 238720, 1287296]
+    blob = assets.write_dvs_flat(synth.dvs_weights(spec, 4), spec)
+    assert len(blob) == 4 * total
+    L = _lib.lib()
+    h = C.c_void_p()
+
+    def load(b, **over):
+        d = dvs.dvs_desc(spec)
+        for k, v in over.items():
+            setattr(d, k, v)
+        return L.vdt_model_load_dvs_flat(b, len(b), C.byref(d), 0, C.byref(h))
+
+    assert load(blob[:-4]) == 2                           # one float short
+    assert load(blob, H=30) == 1                          # two pools need H % 4 == 0
+    assert load(blob, k=2) == 1                           # even kernel
+    assert load(blob, T=0) == 1
+    assert load(blob, delta=7) == 5                       # conv1 frame windows: delta 8, 16 or 32
+    assert load(blob, hidden=100) == 5                    # recurrent FC1 width: multiple of 32
+    assert L.vdt_model_load_dvs_flat(blob, len(blob), None, 0, C.byref(h)) == 1
+    assert h.value is None

@@ -215,3 +215,85 @@ def test_dvs_full_size_network_equals_oracle(O, dev):
     for i, (a, b) in enumerate(zip(r["maps"], ref["maps"])):
         assert bits_equal(_np(a).reshape(-1), b), f"stage {i} differs"
     assert np.array_equal(_np(r["pred"]), ref["pred"])
+
+
+# ------------------------------------------- whole network in the C runtime --
+def test_dvs_net_c_runtime_matches_the_reference_kernels(dev):
+    """The reference's own 2x32x32 network loaded from its flat blob
+    (vdt_model_load_dvs_flat) and run by the C++ runtime: the seven stage
+    maps of vdt_infer_trace and the graph path's outputs equal the golden
+    maps of the reference's kernels, bit for bit."""
+    import torch
+    from vdttfs import assets, dvs, nets, synth
+    g = np.load(os.path.join(GOLDEN, "net_dvs_ref.npz"))
+    spec = nets.dvs_ref()
+    blob = assets.write_dvs_flat(synth.dvs_weights(spec, 4, gains=DVS_GAINS), spec)
+    net = dvs.DvsNet(spec, blob)
+    ctx = net.context(4)
+    frames = _t(g["frames"].astype(np.float32), dev)
+    maps, out, pred = ctx.trace(frames)
+    for i, m in enumerate(maps):
+        assert bits_equal(_np(m).reshape(-1), g[f"map{i}"].astype(np.float32)), f"stage {DvsNet_stage(i)} differs"
+    ref_out = g["map6"].astype(np.float32).reshape(2, spec.classes)
+    want = np.array([np.argmin(o) for o in ref_out])
+    assert np.array_equal(_np(pred), want)
+    o2, p2 = ctx.infer(frames)                                 # captured graph
+    assert bits_equal(_np(o2), ref_out) and np.array_equal(_np(p2), want)
+    ctx.close()
+    net.close()
+
+
+def DvsNet_stage(i):
+    from vdttfs import dvs
+    return dvs.DvsNet.STAGES[i]
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_dvs_net_host_paths_equal_device_path(dev, graphs):
+    """vdt_infer_host and the pipelined vdt_infer_host_batches on a task-3
+    model give vdt_infer's outputs and predictions for every batch, with and
+    without CUDA graphs; a smaller batch than the context's maximum works."""
+    import torch
+    from vdttfs import dvs, nets, synth
+    spec = nets.dvs_ref()
+    net = dvs.DvsNet(spec, synth.dvs_weights(spec, 4))
+    ctx = net.context(5, graphs=graphs)
+    frames = [torch.from_numpy(synth.dvs_frames(4, 3, spec, stream=60 + i)).pin_memory() for i in range(3)]
+    refs = []
+    for f in frames:
+        o, p = ctx.infer(f.to(dev))
+        refs.append((_np(o), _np(p)))
+    for i, f in enumerate(frames):
+        o, p = ctx.infer_host(f)
+        assert bits_equal(o, refs[i][0]) and np.array_equal(p, refs[i][1]), f"infer_host batch {i}"
+    outs, preds = ctx.infer_host_batches(frames)
+    for i in range(3):
+        assert bits_equal(outs[i], refs[i][0]) and np.array_equal(preds[i], refs[i][1]), f"pipelined batch {i}"
+    # the per-stage Python pipeline agrees with the C runtime
+    r = dvs.run(spec, dvs.DvsWeights(spec, synth.dvs_weights(spec, 4), dev), frames[0].to(dev))
+    assert bits_equal(_np(r["out"]), refs[0][0])
+    ctx.close()
+    net.close()
+
+
+def test_dvs_net_profiling_and_unsupported_calls(dev):
+    """Profiling times the seven stages; per-layer integrator choice, LUT
+    reads and sub-batches are refused on a task-3 model."""
+    import torch
+    from vdttfs import dvs, engine as E, nets, synth
+    spec = nets.dvs_ref()
+    net = dvs.DvsNet(spec, synth.dvs_weights(spec, 4))
+    ctx = net.context(2)
+    ctx.set_profiling(True)
+    ctx.layer_times()
+    ctx.infer(torch.from_numpy(synth.dvs_frames(4, 2, spec, stream=3)).to(dev))
+    bkt, comp, nb = ctx.layer_times()
+    assert nb == 1 and (comp > 0).all()
+    assert bkt[dvs.DvsNet.STAGES.index("fc1")] > 0 and bkt[dvs.DvsNet.STAGES.index("fc2")] > 0
+    ctx.set_profiling(False)
+    for call in (lambda: ctx.set_sub_batches(2), lambda: ctx.layer_kernels(), lambda: ctx.set_layer_kernel(0, 1)):
+        with pytest.raises(E.VdtError) as ei:
+            call()
+        assert ei.value.status == 5
+    ctx.close()
+    net.close()

@@ -1,10 +1,13 @@
 """vdt_conv_layer_noalloc (the allocation-free layer step) against the
-allocating per-stage entry points vdt_bucketize + vdt_conv_bucketed.
+allocating per-stage entry points vdt_bucketize + vdt_conv_bucketed and
+against the CPU oracle's bucketize + conv_bucketed (the reference's
+k_bucketize / k_conv_bucketed restated, oracle/oracle.py).
 
 The file name sorts last so that the test also runs after every other test
 in the same process; it passes alone in a fresh process too.  Tolerance:
-none -- both paths run the same bucketing and integrator kernels, so the
-first-spike times must agree bit for bit.
+none -- both GPU paths run the same bucketing and integrator kernels, and
+all three use the same host-libm LUTs, so the first-spike times must agree
+bit for bit.
 """
 import ctypes as C
 
@@ -29,6 +32,7 @@ LAYERS = [
 
 def _setup(case, seed):
     import torch
+    import oracle as O
     from vdttfs import engine as E
     rng = np.random.default_rng(seed)
     B, H, W, Ci, Co, K = case["B"], case["H"], case["W"], case["C_in"], case["C_out"], case["K"]
@@ -39,11 +43,24 @@ def _setup(case, seed):
     bias = (rng.standard_normal(Co) * 0.01).astype(np.float32)
     T = case["T"]
     cfg = E.time_cfg_raw(T, case["delta"], case["tfs"], case["lut_mode"])
-    ld, lt = E.update_LUTs(T, cfg.decay_len, 34.75, 0.0, 34.75, 0.0)
+    hd, hth = O.update_luts(T, cfg.decay_len, 34.75, 0.0, 34.75, 0.0)     # the reference's libm tables
     dev = torch.device("cuda:0")
     t = lambda a: torch.from_numpy(a).to(dev)
-    xs = [t(spike_map(rng, (B, H, W, Ci), fire=0.4, T=T, edges=True)) for _ in range(2)]
-    return dict(Wt=t(Wt), bias=t(bias), ld=ld, lt=lt, cfg=cfg, Ho=Ho, Wo=Wo, xs=xs)
+    hx = [spike_map(rng, (B, H, W, Ci), fire=0.4, T=T, edges=True) for _ in range(2)]
+    return dict(Wt=t(Wt), bias=t(bias), ld=t(hd), lt=t(hth), cfg=cfg, Ho=Ho, Wo=Wo, xs=[t(x) for x in hx],
+                hx=hx, hW=Wt, hb=bias, hd=hd, hth=hth)
+
+
+def _oracle(case, s, hx):
+    import oracle as O
+    B, H, W, Ci = case["B"], case["H"], case["W"], case["C_in"]
+    n_cols = B if case["is_fc"] else B * H * W
+    cfg = s["cfg"]
+    off, cin, tin, _ = O.bucketize(hx, n_cols, Ci, cfg.T, cfg.delta, cfg.fire_start, case["tb_mode"])
+    out, _ = O.conv_bucketed(off, cin, tin, s["hW"], s["hb"], s["hd"], s["hth"], 0, B, H, W, Ci, s["Ho"], s["Wo"],
+                             case["C_out"], case["K"], case["pad"], case["is_fc"], cfg.T, cfg.delta,
+                             cfg.fire_start, cfg.lut_mode)
+    return out
 
 
 def _allocating(case, s, x):
@@ -66,21 +83,23 @@ def _noalloc(case, s, x, out):
 
 
 @pytest.mark.parametrize("case", LAYERS, ids=["conv_stagger", "conv_lenet", "fc"])
-def test_noalloc_matches_allocating_entry_points_twice(case):
+def test_noalloc_matches_allocating_entry_points_and_oracle_twice(case):
     import torch
     from vdttfs._lib import VDT_OK
     s = _setup(case, seed=17 + case["C_out"])
     n_out = case["B"] * s["Ho"] * s["Wo"] * case["C_out"]
     # two calls in a row on different inputs: the second must not see the first's lists
-    for x in s["xs"]:
+    for x, hx in zip(s["xs"], s["hx"]):
         out = torch.full((n_out,), -1.0, dtype=torch.float32, device=x.device)
         assert _noalloc(case, s, x, out) == VDT_OK
         ref = _allocating(case, s, x)
         torch.cuda.synchronize()
         a, b = out.cpu().numpy(), ref.cpu().numpy()
-        assert bits_equal(a, b), f"{np.sum(a != b)} of {b.size} spike times differ"
+        assert bits_equal(a, b), f"{np.sum(a != b)} of {b.size} spike times differ from the allocating path"
+        c = _oracle(case, s, hx)
+        assert bits_equal(a, c), f"{np.sum(a != c)} of {c.size} spike times differ from the oracle"
         assert not (a == -1.0).any(), "every output neuron is written"
-        assert np.mean(b < INF) < 1.0
+        assert 0.0 < np.mean(c < INF) < 1.0
 
 
 def test_noalloc_rejects_a_layer_above_the_scratch_size():

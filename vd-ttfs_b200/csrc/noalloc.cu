@@ -10,13 +10,20 @@
 // the process exits.  The caller passes every input and output.
 //
 // In host code the array's name is only a stand-in for the device symbol, so
-// its device address is looked up with cudaGetSymbolAddress, once per device,
-// on that device's first call (the caller's current device).  That first call
-// should come before any stream capture.  All calls on one device share the
-// array, so calls that can overlap on the GPU race on it.  Nothing in it has
-// to start at zero: the counting sort writes every chunk offset the
-// integrator reads, and the integrator reads only list entries those offsets
-// cover, written by the sort of the same call.
+// its device address is looked up with cudaGetSymbolAddress, with the device
+// current, on the first call on each device (the caller's current device);
+// that first call should come before any stream capture.  The address
+// belongs to the module as loaded into one CUDA context: after
+// cudaDeviceReset the device gets a new context, the module is loaded again
+// and the array may move, so the cached address is keyed by the id of the
+// context it was looked up in (cuCtxGetId, unique for the life of the
+// process) and looked up again when the current context's id differs.  All
+// calls on one device share the array, so calls that can overlap on the GPU
+// race on it.  Nothing in it has to start at zero: the counting sort writes
+// every chunk offset the integrator reads, and the integrator reads only list
+// entries those offsets cover, written by the sort of the same call.
+#include <cuda.h>   // CUcontext / CUresult of the two driver entry points below
+
 #include <mutex>
 
 #include "vdt_internal.h"
@@ -30,22 +37,59 @@ __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchSlot {
+    unsigned long long ctx_id = 0;   // context the address was looked up in
+    void* addr = nullptr;
+};
+ScratchSlot g_scratch[kMaxDevices];
 
-// device address of the scratch array on the current device
+// cuCtxGetCurrent / cuCtxGetId, reached through the runtime (the library
+// links the runtime only)
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+CtxGetCurrentFn g_ctx_current = nullptr;
+CtxGetIdFn g_ctx_id = nullptr;
+
+// id of the calling thread's current context; 0 when there is none yet
+cudaError_t current_context_id(unsigned long long* id) {
+    *id = 0;
+    if (!g_ctx_current || !g_ctx_id) {
+        cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = q1;
+        void* f1 = nullptr;
+        void* f2 = nullptr;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f1, 12000, cudaEnableDefault, &q1);
+        if (e == cudaSuccess) e = cudaGetDriverEntryPointByVersion("cuCtxGetId", &f2, 12000, cudaEnableDefault, &q2);
+        if (e != cudaSuccess) return e;
+        if (q1 != cudaDriverEntryPointSuccess || q2 != cudaDriverEntryPointSuccess || !f1 || !f2)
+            return cudaErrorNotSupported;
+        g_ctx_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+        g_ctx_id = reinterpret_cast<CtxGetIdFn>(f2);
+    }
+    CUcontext ctx = nullptr;
+    if (g_ctx_current(&ctx) != CUDA_SUCCESS) return cudaErrorContextIsDestroyed;
+    if (ctx && g_ctx_id(ctx, id) != CUDA_SUCCESS) return cudaErrorContextIsDestroyed;
+    return cudaSuccess;
+}
+
+// device address of the scratch array in the current device's current context
 cudaError_t scratch_address(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    unsigned long long id = 0;
+    if ((e = current_context_id(&id)) != cudaSuccess) return e;
+    ScratchSlot& slot = g_scratch[dev];
+    if (!slot.addr || id == 0 || slot.ctx_id != id) {
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);    // also makes the context current
         if (e != cudaSuccess) return e;
-        g_scratch_addr[dev] = p;
+        if (id == 0 && (e = current_context_id(&id)) != cudaSuccess) return e;
+        slot.ctx_id = id;
+        slot.addr = p;
     }
-    *out = g_scratch_addr[dev];
+    *out = slot.addr;
     return cudaSuccess;
 }
 

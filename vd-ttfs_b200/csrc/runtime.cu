@@ -23,6 +23,7 @@
 #include <tuple>
 #include <vector>
 
+#include "engine_types.h"
 #include "vdt_internal.h"
 
 using namespace vdt;
@@ -131,17 +132,6 @@ int api_check_cfg(const vdt_time_cfg* c) { return check_cfg(c); }
 
 namespace {
 
-struct Layer {
-    vdt_layer_desc d;
-    int H_in, W_in, C_in, H_out, W_out, C_out;
-    float tc_fire, td;
-    int t_min;
-    float* W = nullptr;      // into the model's weight arena
-    float* bias = nullptr;
-    float* decay = nullptr;  // [decay_len]
-    float* th = nullptr;     // [T]
-};
-
 // Blob reader with bounds checks (the reference's load_weights has none).
 struct Reader {
     const unsigned char* p;
@@ -161,69 +151,6 @@ struct Reader {
 };
 
 }  // namespace
-
-struct vdt_model {
-    int device = 0;
-    vdt_time_cfg cfg{};
-    vdt_net_desc net{};
-    std::vector<Layer> layers;
-    float* arena = nullptr;
-    size_t weight_bytes = 0;
-    int n_classes = 0;
-};
-
-struct GraphKey {
-    int batch, pixels, counting, slot;
-    bool operator<(const GraphKey& o) const {
-        return std::tie(batch, pixels, counting, slot) < std::tie(o.batch, o.pixels, o.counting, o.slot);
-    }
-};
-
-struct vdt_ctx {
-    const vdt_model* m = nullptr;  // must outlive the ctx
-    int device = 0;
-    int max_batch = 0;
-    cudaStream_t stream = nullptr;
-    float* act[3] = {nullptr, nullptr, nullptr};
-    float* in_slot = nullptr;    // [max_batch, in_h, in_w, in_c]
-    float* out_slot = nullptr;   // [max_batch, classes]
-    int32_t* pred_slot = nullptr;
-    // second input/output slot, copy stream and events of the pipelined host
-    // path (vdt_infer_host_batches), made on its first call
-    float* in_slot2 = nullptr;
-    float* out_slot2 = nullptr;
-    int32_t* pred_slot2 = nullptr;
-    cudaStream_t copy_stream = nullptr;
-    cudaEvent_t ev_h2d[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
-    // sub-batches (vdt_ctx_set_sub_batches): parts 1.. of a batch run on
-    // their own streams with their own activation and bucket workspaces
-    struct SubWs {
-        float* act[3] = {nullptr, nullptr, nullptr};
-        int* off = nullptr;
-        int* cin = nullptr;
-        float* tin = nullptr;
-        cudaStream_t stream = nullptr;
-        cudaEvent_t join = nullptr;
-    };
-    int n_sub = 1;
-    std::vector<SubWs> sub;                  // n_sub - 1 entries once made
-    cudaEvent_t ev_fork = nullptr;
-    int* off = nullptr;
-    int* cin = nullptr;
-    float* tin = nullptr;
-    unsigned long long* counters = nullptr;  // [events, fetched]
-    bool graphs = true;
-    bool counting = false;
-    bool profiling = false;
-    int dense_max_fan = 1152;        // layers with K*K*C_in up to this use k_dense
-    std::vector<int> kernel_override;  // per layer: -1 automatic, else VDT_KERNEL_*
-    std::map<GraphKey, cudaGraphExec_t> cache;
-    // profiling: (layer, stage, start, stop) per timed launch, read back lazily
-    struct Mark { int layer, stage; cudaEvent_t a, b; };
-    std::vector<Mark> marks;
-    std::vector<cudaEvent_t> spare_events;
-    int prof_batches = 0;
-};
 
 namespace {
 // which integrator runs a layer: k_thread for narrow conv layers (a warp per
@@ -245,29 +172,6 @@ int layer_kernel(const vdt_ctx* c, int li, const vdt_time_cfg& cfg) {
     return VDT_KERNEL_CHUNK;
 }
 
-cudaEvent_t take_event(vdt_ctx* c) {
-    if (!c->spare_events.empty()) {
-        cudaEvent_t e = c->spare_events.back();
-        c->spare_events.pop_back();
-        return e;
-    }
-    cudaEvent_t e = nullptr;
-    cudaEventCreate(&e);
-    return e;
-}
-struct StageTimer {  // records a start/stop pair around one stage when profiling
-    vdt_ctx* c; int layer, stage; cudaEvent_t a = nullptr;
-    StageTimer(vdt_ctx* c_, int l, int s) : c(c_), layer(l), stage(s) {
-        if (c->profiling) { a = take_event(c); cudaEventRecord(a, c->stream); }
-    }
-    ~StageTimer() {
-        if (a) {
-            cudaEvent_t b = take_event(c);
-            cudaEventRecord(b, c->stream);
-            c->marks.push_back({layer, stage, a, b});
-        }
-    }
-};
 }  // namespace
 
 // ----------------------------------------------------------------- metadata
@@ -395,7 +299,10 @@ extern "C" int vdt_model_load_blob(const void* blob, size_t nbytes, const vdt_la
         hb.push_back(bp);
     }
     if (r.off != r.n) { delete m; return fail(VDT_ERR_BLOB, "blob has %zu trailing bytes", r.n - r.off); }
-    m->n_classes = m->layers.back().C_out;
+    // the output is the last map, flattened (an FC layer's [classes]; a conv
+    // layer's pooled or unpooled [H, W, C])
+    m->n_classes = h * w * c;
+    m->in_elems = (size_t)net->in_h * net->in_w * net->in_c;
 
     DeviceGuard g(device);
     if (!g.ok) { delete m; return fail(VDT_ERR_CUDA, "cannot select device %d", device); }
@@ -452,13 +359,14 @@ extern "C" void vdt_model_destroy(vdt_model* m) {
 
 extern "C" int vdt_model_info(const vdt_model* m, int* n_layers, int* n_classes, size_t* wbytes) {
     if (!m) return fail(VDT_ERR_INVALID, "model is NULL");
-    if (n_layers) *n_layers = (int)m->layers.size();
+    if (n_layers) *n_layers = model_stages(m);
     if (n_classes) *n_classes = m->n_classes;
     if (wbytes) *wbytes = m->weight_bytes;
     return VDT_OK;
 }
 
 extern "C" int vdt_model_luts(const vdt_model* m, int layer, float* h_decay, float* h_th) {
+    if (m && m->is_dvs) return fail(VDT_ERR_UNSUPPORTED, "a task-3 network has no LUTs");
     if (!m || layer < 0 || layer >= (int)m->layers.size()) return fail(VDT_ERR_INVALID, "bad layer");
     DeviceGuard g(m->device);
     const Layer& ly = m->layers[layer];
@@ -478,7 +386,12 @@ Sizes ctx_sizes(const vdt_model* m, long long B) {
     Sizes s;
     const int dmin = std::min(m->cfg.delta, kSortedDelta);
     const int OS = (m->cfg.T + dmin - 1) / dmin + 1;
-    s.act = (size_t)B * m->net.in_h * m->net.in_w * m->net.in_c;
+    if (m->is_dvs) {
+        const DvsSizes d = dvs_sizes(m, B);
+        s.act = d.act; s.off = d.off; s.bkt = d.bkt;
+        return s;
+    }
+    s.act = (size_t)B * m->in_elems;
     for (auto& ly : m->layers) {
         const size_t in = (size_t)B * ly.H_in * ly.W_in * ly.C_in;
         const size_t out = (size_t)B * ly.H_out * ly.W_out * ly.C_out;
@@ -515,13 +428,14 @@ void ctx_free(vdt_ctx* c) {
     }
     c->sub.clear();
     if (c->ev_fork) cudaEventDestroy(c->ev_fork);
-    cudaFree(c->off); cudaFree(c->cin); cudaFree(c->tin); cudaFree(c->counters);
+    cudaFree(c->off); cudaFree(c->cin); cudaFree(c->tin); cudaFree(c->scratch); cudaFree(c->counters);
 }
 
 // Enqueue one batch: the reference's per-batch layer sequence.
 int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, int32_t* d_pred,
             float* const* trace) {
     const vdt_model* m = c->m;
+    if (m->is_dvs) return dvs_enqueue(c, d_input, B, d_out, d_pred, trace);
     const vdt_time_cfg& cfg = m->cfg;
     cudaStream_t s = c->stream;
     const float* x = d_input;
@@ -533,11 +447,12 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
         x = c->act[0];
         ai = 1;
     }
-    unsigned long long* ev = c->counting ? c->counters : nullptr;
-    unsigned long long* fe = c->counting ? c->counters + 1 : nullptr;
     const int L = (int)m->layers.size();
     for (int i = 0; i < L; ++i) {
         const Layer& ly = m->layers[i];
+        // layer i counts into counters[2i] (events) and [2i + 1] (fetched synapses)
+        unsigned long long* ev = c->counting ? c->counters + 2 * i : nullptr;
+        unsigned long long* fe = c->counting ? c->counters + 2 * i + 1 : nullptr;
         const bool last = i == L - 1;
         float* y = (last && !ly.d.pool_after) ? d_out : c->act[ai];
         if (trace && trace[i] && !last) y = trace[i];
@@ -639,7 +554,7 @@ int enqueue_split(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_
     const int n = std::min(c->n_sub, B);
     if (n < 2 || c->counting || c->profiling) return enqueue(c, d_input, pixels, B, d_out, d_pred, nullptr);
     const vdt_model* m = c->m;
-    const size_t in_row = (size_t)m->net.in_h * m->net.in_w * m->net.in_c;
+    const size_t in_row = m->in_elems;
     cudaStream_t s = c->stream;
     VDT_CUDA(cudaEventRecord(c->ev_fork, s));
     auto swap_ws = [c](vdt_ctx::SubWs& w) {
@@ -678,6 +593,7 @@ extern "C" int vdt_ctx_set_sub_batches(vdt_ctx* c, int n) {
     g_last_error.clear();
     if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
     if (n < 1 || n > VDT_MAX_SUB_BATCHES) return fail(VDT_ERR_INVALID, "n=%d (1 to %d)", n, VDT_MAX_SUB_BATCHES);
+    if (c->m->is_dvs && n != 1) return fail(VDT_ERR_UNSUPPORTED, "a task-3 network runs whole batches");
     DeviceGuard g(c->m->device);
     if (!c->ev_fork) VDT_CUDA(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
     const Sizes z = ctx_sizes(c->m, (c->max_batch + n - 1) / n);
@@ -714,7 +630,7 @@ extern "C" int vdt_ctx_create(const vdt_model* m, int max_batch, vdt_stream stre
     c->max_batch = max_batch;
     c->stream = static_cast<cudaStream_t>(stream);
     const Sizes z = ctx_sizes(m, max_batch);
-    const size_t in_n = (size_t)max_batch * m->net.in_h * m->net.in_w * m->net.in_c;
+    const size_t in_n = (size_t)max_batch * m->in_elems;
     cudaError_t e = cudaSuccess;
     for (auto& a : c->act) if (e == cudaSuccess) e = cudaMalloc(&a, z.act * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&c->in_slot, in_n * sizeof(float));
@@ -723,8 +639,13 @@ extern "C" int vdt_ctx_create(const vdt_model* m, int max_batch, vdt_stream stre
     if (e == cudaSuccess) e = cudaMalloc(&c->off, std::max<size_t>(z.off, 1) * sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&c->cin, std::max<size_t>(z.bkt, 1) * sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&c->tin, std::max<size_t>(z.bkt, 1) * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&c->counters, 2 * sizeof(unsigned long long));
-    if (e == cudaSuccess) e = cudaMemset(c->counters, 0, 2 * sizeof(unsigned long long));
+    if (e == cudaSuccess && m->is_dvs) {
+        c->scratch_bytes = dvs_sizes(m, max_batch).scratch_bytes;
+        if (c->scratch_bytes) e = cudaMalloc(&c->scratch, c->scratch_bytes);
+    }
+    const size_t n_counters = 2 * std::max<size_t>(1, m->layers.size());
+    if (e == cudaSuccess) e = cudaMalloc(&c->counters, n_counters * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(c->counters, 0, n_counters * sizeof(unsigned long long));
     if (e != cudaSuccess) {
         ctx_free(c);
         delete c;
@@ -754,15 +675,40 @@ extern "C" int vdt_ctx_set_counting(vdt_ctx* c, int enable) {
     return VDT_OK;
 }
 
-extern "C" int vdt_ctx_counters(vdt_ctx* c, unsigned long long* events, unsigned long long* fetched) {
-    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+// Per-layer counts since the last read, then zeroed.
+static int read_counters(vdt_ctx* c, std::vector<unsigned long long>& h) {
     DeviceGuard g(c->m->device);
-    unsigned long long h[2];
+    h.assign(2 * std::max<size_t>(1, c->m->layers.size()), 0ull);
     VDT_CUDA(cudaStreamSynchronize(c->stream));
-    VDT_CUDA(cudaMemcpy(h, c->counters, sizeof h, cudaMemcpyDeviceToHost));
-    if (events) *events = h[0];
-    if (fetched) *fetched = h[1];
-    VDT_CUDA(cudaMemset(c->counters, 0, sizeof h));
+    VDT_CUDA(cudaMemcpy(h.data(), c->counters, h.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+    VDT_CUDA(cudaMemset(c->counters, 0, h.size() * sizeof(unsigned long long)));
+    return VDT_OK;
+}
+
+extern "C" int vdt_ctx_counters(vdt_ctx* c, unsigned long long* events, unsigned long long* fetched) {
+    g_last_error.clear();
+    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    std::vector<unsigned long long> h;
+    if (int s = read_counters(c, h)) return s;
+    unsigned long long ev = 0, fe = 0;
+    for (size_t i = 0; i + 1 < h.size(); i += 2) { ev += h[i]; fe += h[i + 1]; }
+    if (events) *events = ev;
+    if (fetched) *fetched = fe;
+    return VDT_OK;
+}
+
+extern "C" int vdt_ctx_layer_counters(vdt_ctx* c, int n_layers, unsigned long long* events,
+                                      unsigned long long* fetched) {
+    g_last_error.clear();
+    if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    if (c->m->is_dvs) return fail(VDT_ERR_UNSUPPORTED, "a task-3 network has no event counters");
+    if (n_layers != (int)c->m->layers.size()) return fail(VDT_ERR_INVALID, "n_layers mismatch");
+    std::vector<unsigned long long> h;
+    if (int s = read_counters(c, h)) return s;
+    for (int i = 0; i < n_layers; ++i) {
+        if (events) events[i] = h[2 * i];
+        if (fetched) fetched[i] = h[2 * i + 1];
+    }
     return VDT_OK;
 }
 
@@ -775,7 +721,7 @@ extern "C" int vdt_ctx_set_profiling(vdt_ctx* c, int enable) {
 extern "C" int vdt_ctx_layer_times(vdt_ctx* c, int n_layers, float* bkt_ms, float* int_ms,
                                    float* pool_ms, int* batches) {
     if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
-    if (n_layers != (int)c->m->layers.size()) return fail(VDT_ERR_INVALID, "n_layers mismatch");
+    if (n_layers != model_stages(c->m)) return fail(VDT_ERR_INVALID, "n_layers mismatch");
     DeviceGuard g(c->m->device);
     VDT_CUDA(cudaStreamSynchronize(c->stream));
     float* dst[3] = {bkt_ms, int_ms, pool_ms};
@@ -796,6 +742,7 @@ extern "C" int vdt_ctx_layer_times(vdt_ctx* c, int n_layers, float* bkt_ms, floa
 extern "C" int vdt_ctx_layer_kernels(const vdt_ctx* c, int n_layers, int* kernels) {
     g_last_error.clear();
     if (!c || !kernels) return fail(VDT_ERR_INVALID, "ctx or kernels is NULL");
+    if (c->m->is_dvs) return fail(VDT_ERR_UNSUPPORTED, "a task-3 network has no per-layer integrator choice");
     if (n_layers != (int)c->m->layers.size()) return fail(VDT_ERR_INVALID, "n_layers mismatch");
     for (int i = 0; i < n_layers; ++i) kernels[i] = layer_kernel(c, i, c->m->cfg);
     return VDT_OK;
@@ -804,6 +751,7 @@ extern "C" int vdt_ctx_layer_kernels(const vdt_ctx* c, int n_layers, int* kernel
 extern "C" int vdt_ctx_set_layer_kernel(vdt_ctx* c, int layer, int kernel) {
     g_last_error.clear();
     if (!c) return fail(VDT_ERR_INVALID, "ctx is NULL");
+    if (c->m->is_dvs) return fail(VDT_ERR_UNSUPPORTED, "a task-3 network has no per-layer integrator choice");
     if (layer < 0 || layer >= (int)c->m->layers.size()) return fail(VDT_ERR_INVALID, "layer=%d", layer);
     const Layer& ly = c->m->layers[layer];
     const vdt_time_cfg& cfg = c->m->cfg;
@@ -884,7 +832,7 @@ extern "C" int vdt_infer(vdt_ctx* c, const float* d_input, int input_is_pixels, 
     if (int s = check_device_buffers(c->m->device, {d_input, d_out, d_pred})) return s;
     DeviceGuard g(c->m->device);
     const vdt_model* m = c->m;
-    const size_t in_n = (size_t)batch * m->net.in_h * m->net.in_w * m->net.in_c;
+    const size_t in_n = (size_t)batch * m->in_elems;
     if (!c->graphs || c->profiling) return enqueue_split(c, d_input, input_is_pixels, batch, d_out, d_pred);
     VDT_CUDA(cudaMemcpyAsync(c->in_slot, d_input, in_n * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
     if (int s = run_slots(c, input_is_pixels, batch)) return s;
@@ -903,7 +851,7 @@ extern "C" int vdt_infer_host(vdt_ctx* c, const float* h_input, int input_is_pix
     if (!h_input) return fail(VDT_ERR_INVALID, "h_input is NULL");
     DeviceGuard g(c->m->device);
     const vdt_model* m = c->m;
-    const size_t in_n = (size_t)batch * m->net.in_h * m->net.in_w * m->net.in_c;
+    const size_t in_n = (size_t)batch * m->in_elems;
     VDT_CUDA(cudaMemcpyAsync(c->in_slot, h_input, in_n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     if (c->graphs) {
         if (int s = run_slots(c, input_is_pixels, batch)) return s;
@@ -924,7 +872,7 @@ extern "C" int vdt_infer_host(vdt_ctx* c, const float* h_input, int input_is_pix
 static int ensure_pipeline(vdt_ctx* c) {
     if (c->copy_stream) return VDT_OK;
     const vdt_model* m = c->m;
-    const size_t in_n = (size_t)c->max_batch * m->net.in_h * m->net.in_w * m->net.in_c;
+    const size_t in_n = (size_t)c->max_batch * m->in_elems;
     cudaError_t e = cudaMalloc(&c->in_slot2, in_n * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&c->out_slot2, (size_t)c->max_batch * m->n_classes * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&c->pred_slot2, (size_t)c->max_batch * sizeof(int32_t));
@@ -951,7 +899,7 @@ extern "C" int vdt_infer_host_batches(vdt_ctx* c, int n_batches, const float* co
     DeviceGuard g(c->m->device);
     if (int s = ensure_pipeline(c)) return s;
     const vdt_model* m = c->m;
-    const size_t in_bytes = (size_t)batch * m->net.in_h * m->net.in_w * m->net.in_c * sizeof(float);
+    const size_t in_bytes = (size_t)batch * m->in_elems * sizeof(float);
     const size_t out_bytes = (size_t)batch * m->n_classes * sizeof(float);
     const size_t pred_bytes = (size_t)batch * sizeof(int32_t);
     float* const ins[2] = {c->in_slot, c->in_slot2};
@@ -990,7 +938,7 @@ extern "C" int vdt_infer_trace(vdt_ctx* c, const float* d_input, int input_is_pi
     if (int s = check_batch(c, batch)) return s;
     if (!d_input || !d_out || !d_layer_out) return fail(VDT_ERR_INVALID, "NULL buffer");
     if (int s = check_device_buffers(c->m->device, {d_input, d_out, d_pred})) return s;
-    for (size_t i = 0; i < c->m->layers.size(); ++i)
+    for (int i = 0; i < model_stages(c->m); ++i)
         if (int s = check_device_buffers(c->m->device, {d_layer_out[i]})) return s;
     DeviceGuard g(c->m->device);
     return enqueue(c, d_input, input_is_pixels, batch, d_out, d_pred, d_layer_out);

@@ -37,6 +37,13 @@ class NetDesc(C.Structure):
                 ("readout", C.c_int)]
 
 
+class DvsDesc(C.Structure):
+    _fields_ = [("in_c", C.c_int), ("H", C.c_int), ("W", C.c_int), ("T", C.c_int), ("delta", C.c_int),
+                ("c1", C.c_int), ("c2", C.c_int), ("c3", C.c_int), ("k", C.c_int), ("hidden", C.c_int),
+                ("classes", C.c_int), ("decay_conv", C.c_float), ("th_conv", C.c_float),
+                ("decay_fc", C.c_float), ("th_fc", C.c_float)]
+
+
 # every function the header declares: name -> (restype, argtypes)
 _vp, _fp, _ip = C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int)
 SIGNATURES = {
@@ -46,6 +53,8 @@ SIGNATURES = {
     "vdt_model_load_blob": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(LayerDesc), C.c_int,
                                       C.POINTER(NetDesc), C.POINTER(TimeCfg), C.c_int,
                                       C.POINTER(C.c_void_p)]),
+    "vdt_model_load_dvs_flat": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(DvsDesc), C.c_int,
+                                          C.POINTER(C.c_void_p)]),
     "vdt_model_destroy": (None, [_vp]),
     "vdt_model_info": (C.c_int, [_vp, _ip, _ip, C.POINTER(C.c_size_t)]),
     "vdt_model_luts": (C.c_int, [_vp, C.c_int, _vp, _vp]),
@@ -54,6 +63,7 @@ SIGNATURES = {
     "vdt_ctx_set_graphs": (C.c_int, [_vp, C.c_int]),
     "vdt_ctx_set_counting": (C.c_int, [_vp, C.c_int]),
     "vdt_ctx_counters": (C.c_int, [_vp, C.POINTER(C.c_ulonglong), C.POINTER(C.c_ulonglong)]),
+    "vdt_ctx_layer_counters": (C.c_int, [_vp, C.c_int, _vp, _vp]),
     "vdt_ctx_set_profiling": (C.c_int, [_vp, C.c_int]),
     "vdt_ctx_layer_times": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _ip]),
     "vdt_infer": (C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp, _vp]),
@@ -89,6 +99,7 @@ SIGNATURES = {
     "vdt_dvs_fc2": (C.c_int, [_vp] * 4 + [C.c_int] * 5 + [C.c_float, C.c_float, _vp, _vp]),
     "vdt_oihw_to_hwio": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, _vp]),
     "vdt_set_launch_overlap": (C.c_int, [C.c_int]),
+    "vdt_measure_peaks": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "vdt_noalloc_scratch_bytes": (C.c_size_t, []),
     "vdt_conv_layer_noalloc": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, C.c_int, C.c_int,
                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,

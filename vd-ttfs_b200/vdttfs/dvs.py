@@ -18,12 +18,13 @@ from __future__ import annotations
 
 import ctypes as C
 import dataclasses
+import weakref
 
 import numpy as np
 
 from . import nets
-from ._lib import TimeCfg, check, lib
-from .engine import LAYOUT_NCHW, LAYOUT_NHWC, TB_TRUNC, _ptr, _stream, bucketize, readout
+from ._lib import DvsDesc, TimeCfg, check, lib
+from .engine import LAYOUT_NCHW, LAYOUT_NHWC, TB_TRUNC, Context, _ptr, _stream, bucketize, readout
 
 
 def _cfg(spec: nets.DvsSpec) -> TimeCfg:
@@ -43,6 +44,91 @@ class DvsWeights:
         self.fc1_t = t(np.asarray(wts["fc1"]).T)                # [F_in, hidden]
         self.rec_t = t(np.asarray(wts["fc1_rec"]).T)            # [hidden, hidden], [j][i]
         self.fc2_t = t(np.asarray(wts["fc2"]).T)                # [hidden, classes]
+
+
+def dvs_desc(spec: nets.DvsSpec) -> DvsDesc:
+    """The C ABI's vdt_dvs_desc of a network spec."""
+    c1, c2, c3 = spec.convs
+    return DvsDesc(spec.in_c, spec.H, spec.W, spec.T, spec.delta, c1, c2, c3, spec.k, spec.hidden,
+                   spec.classes, spec.decay_conv, spec.th_conv, spec.decay_fc, spec.th_fc)
+
+
+class DvsNet:
+    """The whole task-3 network as one engine model: the reference's flat
+    weight blob (t3:237-241; `weights` is the blob's bytes or the dict of
+    synth.dvs_weights / assets.load_dvs_flat) loaded by
+    vdt_model_load_dvs_flat, run per batch by the C++ runtime (one captured
+    CUDA graph per batch size, workspace owned by the context)."""
+
+    STAGES = ("conv1", "conv2", "pool1", "conv3", "pool2", "fc1", "fc2")
+
+    def __init__(self, spec: nets.DvsSpec, weights, device: int = 0):
+        from .assets import write_dvs_flat
+        self.spec = spec
+        blob = bytes(weights) if isinstance(weights, (bytes, bytearray, memoryview)) else write_dvs_flat(weights, spec)
+        self._desc = dvs_desc(spec)
+        h = C.c_void_p()
+        check(lib().vdt_model_load_dvs_flat(blob, len(blob), C.byref(self._desc), device, C.byref(h)),
+              "vdt_model_load_dvs_flat")
+        self.h = h
+        self.device = device
+        self.n_classes = spec.classes
+        self._contexts = weakref.WeakSet()
+
+    def context(self, max_batch: int, stream=None, graphs: bool = True) -> "DvsContext":
+        return DvsContext(self, max_batch, stream=stream, graphs=graphs)
+
+    def stage_shapes(self, N: int):
+        s = self.spec
+        c1, c2, c3 = s.convs
+        return [(N, c1, s.H, s.W), (N, c2, s.H, s.W), (N, c2, s.H // 2, s.W // 2), (N, c3, s.H // 2, s.W // 2),
+                (N, c3, s.H // 4, s.W // 4), (N, s.hidden), (N, s.classes)]
+
+    def close(self):
+        if self.h:
+            for c in list(self._contexts):
+                c.close()
+            lib().vdt_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DvsContext(Context):
+    """Per-stream workspace of a DvsNet.  infer / infer_host /
+    infer_host_batches take frames [N, C, H, W, T] (time innermost) and return
+    FC2's first-spike times [N, classes] and the argmin readout."""
+
+    def layer_times(self):
+        """Per stage (DvsNet.STAGES) the bucketize and compute milliseconds
+        accumulated since the last call, and the number of batches."""
+        n = len(DvsNet.STAGES)
+        a, b, c = (np.zeros(n, np.float32) for _ in range(3))
+        nb = C.c_int()
+        check(lib().vdt_ctx_layer_times(self.h, n, a.ctypes.data, b.ctypes.data, c.ctypes.data,
+                                        C.byref(nb)), "vdt_ctx_layer_times")
+        return a, b, nb.value
+
+    def layer_kernels(self):
+        """Raises VdtError (VDT_ERR_UNSUPPORTED): the stages' kernels are fixed."""
+        k = np.zeros(len(DvsNet.STAGES), np.int32)
+        check(lib().vdt_ctx_layer_kernels(self.h, len(k), k.ctypes.data), "vdt_ctx_layer_kernels")
+        return [int(v) for v in k]
+
+    def trace(self, frames):
+        """The whole network, returning every stage's output map."""
+        import torch
+        N = frames.shape[0]
+        maps = [torch.empty(s, dtype=torch.float32, device=frames.device) for s in self.model.stage_shapes(N)]
+        arr = (C.c_void_p * len(maps))(*[_ptr(m) for m in maps])
+        out = torch.empty((N, self.model.n_classes), dtype=torch.float32, device=frames.device)
+        pred = torch.empty((N,), dtype=torch.int32, device=frames.device)
+        check(lib().vdt_infer_trace(self.h, _ptr(frames), 0, N, arr, _ptr(out), _ptr(pred)), "vdt_infer_trace")
+        return maps, out, pred
 
 
 def oihw_to_hwio(w, stream=None):

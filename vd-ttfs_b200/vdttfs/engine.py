@@ -134,6 +134,14 @@ class Context:
         check(lib().vdt_ctx_counters(self.h, C.byref(e), C.byref(f)), "vdt_ctx_counters")
         return e.value, f.value
 
+    def layer_counters(self):
+        """Per layer (events kept by its bucketing, synapses its integrator
+        fetched) since the last read of either counter call."""
+        n = len(self.model.net.layers)
+        e, f = np.zeros(n, np.uint64), np.zeros(n, np.uint64)
+        check(lib().vdt_ctx_layer_counters(self.h, n, e.ctypes.data, f.ctypes.data), "vdt_ctx_layer_counters")
+        return [int(v) for v in e], [int(v) for v in f]
+
     def set_profiling(self, on: bool):
         check(lib().vdt_ctx_set_profiling(self.h, int(on)), "vdt_ctx_set_profiling")
 

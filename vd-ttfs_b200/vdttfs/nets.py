@@ -94,7 +94,12 @@ class NetSpec:
 
     @property
     def n_classes(self) -> int:
-        return self.layers[-1].c_out
+        """Output values per image: the last layer's map, flattened (an FC
+        layer's classes; a conv layer's [H, W, C] after its pool, if any)."""
+        _, _, _, ho, wo, co = self.shapes()[-1]
+        if self.layers[-1].pool_after:
+            ho, wo = ho // 2, wo // 2
+        return ho * wo * co
 
     def with_time(self, T: int | None = None, delta: int | None = None) -> "NetSpec":
         T = self.T if T is None else T
