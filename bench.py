@@ -192,15 +192,18 @@ def layer_bytes(net, events_per_layer, B):
 
 
 def launches_per_step(net, kernels, pixels=True):
-    """Kernel launches of one inference: encode, per layer bucketize (not for
-    k_dense / k_thread / k_layer_vmem layers) + integrator, pools (a k_thread
-    layer's pool is fused into it), readout."""
+    """Kernel launches of one inference (graph path, one sub-batch): the
+    pixel encoder; per layer its integrator, plus a bucketize pass unless the
+    integrator reads the spike map itself (k_dense, k_thread, k_layer_vmem),
+    plus a pool pass unless the pool runs fused into the integrator
+    (k_thread); the readout unless the last layer is a membrane readout (it
+    runs fused there).  Each sub-batch launches the same sequence."""
     from vdttfs.engine import KERNEL_DENSE, KERNEL_THREAD, KERNEL_VMEM
     n = 1 if pixels else 0
     for l, k in zip(net.layers, kernels):
         n += 1 if k in (KERNEL_DENSE, KERNEL_THREAD, KERNEL_VMEM) else 2
         n += 1 if l.pool_after and k != KERNEL_THREAD else 0
-    return n + 1        # readout
+    return n + (0 if kernels[-1] == KERNEL_VMEM else 1)
 
 
 # ------------------------------------------------------------------ parity --
@@ -482,7 +485,7 @@ def run_engine(a):
                          "algorithmic_bytes_per_layer": [int(v) for v in lbytes],
                          "fetched_synapses_per_layer": [int(v) for v in fe_layer],
                          "kernels": [f"L{i}:{E.KERNEL_NAMES[k]}" for i, k in enumerate(kernels)]}},
-            "gpu_launches": launches_per_step(net, kernels) * a.steps,
+            "gpu_launches": launches_per_step(net, kernels) * 2 * a.steps,     # two sub-batches per step
             "events_per_image": round(sum(ev_layer) / B, 1),
             "fetched_synapses_per_image": round(sum(fe_layer) / B, 1),
             "clocks": clk,

@@ -122,10 +122,15 @@ __global__ void k_pool_min_scalar(const float* __restrict__ in, float* __restric
     }
 }
 
+// is value v a strict improvement on m for readout `mode`?
+__device__ __forceinline__ bool readout_better(float v, float m, int mode) {
+    return mode == VDT_READ_ARGMAX ? v > m : v < m;
+}
+
 __global__ void k_layer_vmem(const float* __restrict__ in, const float* __restrict__ W,
                              const float* __restrict__ bias, const float* __restrict__ lut,
                              int B, int C_in, int C_out, int T, float tfs, float inf_time,
-                             float* __restrict__ out) {
+                             float* __restrict__ out, int32_t* __restrict__ pred, int mode) {
     extern __shared__ float s_in[];                  // [warps][C_in] values, then flags
     chain_release();
     chain_wait();
@@ -147,11 +152,31 @@ __global__ void k_layer_vmem(const float* __restrict__ in, const float* __restri
         use[i] = u ? 1 : 0;
     }
     __syncwarp();
+    // the readout fused in: each lane scans its own outputs in increasing
+    // index order from k_readout's start value (for ARGMIN_LOWEST: lane 0
+    // starts at output 0, the other lanes at +infinity), then the lanes'
+    // bests merge, a lower index winning a tie -- k_readout's sequential scan
+    // keeps the first index of the best value
+    float m = mode == VDT_READ_ARGMAX ? -1e9f : (mode == VDT_READ_ARGMIN_FIRST ? inf_time : __int_as_float(0x7f800000));
+    int pbest = -1;
     for (int c = lane; c < C_out; c += 32) {
         float acc = 0.0f;
         for (int i = 0; i < C_in; ++i)
             if (use[i]) acc = fmaf(__ldg(W + (long long)i * C_out + c), x[i], acc);
-        out[img * C_out + c] = acc + __ldg(bias + c);
+        const float v = acc + __ldg(bias + c);
+        out[img * C_out + c] = v;
+        if (mode == VDT_READ_ARGMIN_LOWEST && c == 0) { m = v; pbest = 0; }
+        else if (readout_better(v, m, mode)) { m = v; pbest = c; }
+    }
+    if (pred) {
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            const float m2 = __shfl_down_sync(0xffffffffu, m, d);
+            const int p2 = __shfl_down_sync(0xffffffffu, pbest, d);
+            const bool take = p2 >= 0 && (pbest < 0 || readout_better(m2, m, mode) || (m2 == m && p2 < pbest));
+            if (take) { m = m2; pbest = p2; }
+        }
+        if (lane == 0) pred[img] = pbest;
     }
 }
 
@@ -220,13 +245,14 @@ cudaError_t launch_pool_min(const float* in, float* out, int B, int H_in, int W_
 
 cudaError_t launch_layer_vmem(const float* in, const float* W, const float* bias,
                               const float* lut_decay, int B, int C_in, int C_out, int T,
-                              float tfs, float inf_time, float* out, cudaStream_t s) {
+                              float tfs, float inf_time, float* out, cudaStream_t s,
+                              int32_t* pred, int readout) {
     if (B <= 0) return cudaSuccess;
     const int warps = 4;
     const size_t smem = (size_t)warps * C_in * (sizeof(float) + 1);
     if (smem > 48 * 1024) return cudaErrorInvalidValue;
     return launch_chain(k_layer_vmem, dim3((B + warps - 1) / warps), dim3(warps * 32), smem, s, in, W, bias,
-                        lut_decay, B, C_in, C_out, T, tfs, inf_time, out);
+                        lut_decay, B, C_in, C_out, T, tfs, inf_time, out, pred, readout);
 }
 
 cudaError_t launch_readout(const float* out, int B, int K, int mode, float inf_time, int32_t* pred,

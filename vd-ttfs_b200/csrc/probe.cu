@@ -39,19 +39,24 @@ __global__ void k_probe_fma(float* out, int iters, float a, float b) {
     if (s == 12345.678f) out[blockIdx.x] = s;            // keeps the chains live
 }
 
+constexpr int kL2Unroll = 4;   // independent 16-byte loads in flight per thread
+
 // Every thread reads 16-byte vectors of an L2-resident buffer, cached in L2
-// only (ld.global.cg), `reps` passes over its CTA's slice.
-__global__ void k_probe_l2(const float4* __restrict__ buf, long long n_vec, int reps, float* out) {
-    const long long per_cta = n_vec / gridDim.x;
+// only (ld.global.cg), kL2Unroll independent loads at a time, `reps` passes
+// over its CTA's slice (a whole number of blockDim * kL2Unroll vectors).
+__global__ void k_probe_l2(const float4* __restrict__ buf, long long per_cta, int reps, float* out) {
     const float4* p = buf + per_cta * blockIdx.x;
     float s = 0.0f;
     for (int r = 0; r < reps; ++r) {
-        for (long long i = threadIdx.x; i < per_cta; i += blockDim.x) {
-            float4 v;
-            asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
-                         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                         : "l"(p + i));
-            s += v.x + v.y + v.z + v.w;
+        for (long long i = threadIdx.x; i < per_cta; i += (long long)blockDim.x * kL2Unroll) {
+            float4 v[kL2Unroll];
+#pragma unroll
+            for (int u = 0; u < kL2Unroll; ++u)
+                asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+                             : "=f"(v[u].x), "=f"(v[u].y), "=f"(v[u].z), "=f"(v[u].w)
+                             : "l"(p + i + (long long)u * blockDim.x));
+#pragma unroll
+            for (int u = 0; u < kL2Unroll; ++u) s += v[u].x + v[u].y + v[u].z + v[u].w;
         }
     }
     if (s == 12345.678f) out[blockIdx.x] = s;
@@ -81,7 +86,7 @@ extern "C" int vdt_measure_peaks(int device, double* fma_per_s, double* l2_read_
     if (e == cudaSuccess) e = cudaEventCreate(&e0);
     if (e == cudaSuccess) e = cudaEventCreate(&e1);
     const int fma_blocks = sms * 8, fma_threads = 256, iters = 4096;
-    const int l2_blocks = sms * 8, l2_threads = 512, reps = 64;
+    const int l2_blocks = sms * 4, l2_threads = 512, reps = 64;   // 2048 threads per SM
     for (int trial = 0; trial < 4 && e == cudaSuccess; ++trial) {
         float ms = 0.0f;
         cudaEventRecord(e0);
@@ -93,12 +98,14 @@ extern "C" int vdt_measure_peaks(int device, double* fma_per_s, double* l2_read_
             best_fma = std::max(best_fma, 2.0 * kChains * iters * (double)fma_blocks * fma_threads / (ms * 1e-3));
         if (e != cudaSuccess) break;
         const long long n_vec = (long long)(l2_bytes / sizeof(float4));
+        const long long chunk = (long long)l2_threads * kL2Unroll;
+        const long long per_cta = n_vec / l2_blocks / chunk * chunk;
         cudaEventRecord(e0);
-        k_probe_l2<<<l2_blocks, l2_threads>>>(reinterpret_cast<const float4*>(buf), n_vec, reps, out);
+        k_probe_l2<<<l2_blocks, l2_threads>>>(reinterpret_cast<const float4*>(buf), per_cta, reps, out);
         cudaEventRecord(e1);
         e = cudaEventSynchronize(e1);
         if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
-        const double moved = (double)(n_vec / l2_blocks) * l2_blocks * sizeof(float4) * reps;
+        const double moved = (double)per_cta * l2_blocks * sizeof(float4) * reps;
         if (e == cudaSuccess && trial > 0) best_l2 = std::max(best_l2, moved / (ms * 1e-3));
     }
     if (e == cudaSuccess) e = cudaGetLastError();

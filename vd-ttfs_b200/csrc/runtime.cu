@@ -440,6 +440,9 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
     cudaStream_t s = c->stream;
     const float* x = d_input;
     int ai = 0;
+    // pixels: one encode pass writes the spike times first (fusing it into
+    // the first layer's read measured slower: every output pixel re-encodes
+    // each input of its window)
     if (pixels && m->net.encoder != VDT_ENC_NONE) {
         const long long n = (long long)B * m->net.in_h * m->net.in_w * m->net.in_c;
         VDT_CUDA(launch_encode(d_input, c->act[0], n, m->net.encoder, m->net.tc_in, m->net.td_in,
@@ -447,6 +450,7 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
         x = c->act[0];
         ai = 1;
     }
+    bool readout_done = false;                               // the readout ran fused into the last layer
     const int L = (int)m->layers.size();
     for (int i = 0; i < L; ++i) {
         const Layer& ly = m->layers[i];
@@ -459,9 +463,12 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
         if (trace && trace[i] && last && ly.d.pool_after) y = trace[i];
         bool pooled = false;                                 // the layer's pool ran fused into it
         if (ly.d.out == VDT_OUT_VMEM) {
+            // the membrane readout (last layer only) with the argmax fused in
+            int32_t* fused_pred = last ? d_pred : nullptr;
             StageTimer st(c, i, 1);
             VDT_CUDA(launch_layer_vmem(x, ly.W, ly.bias, ly.decay, B, ly.C_in, ly.C_out, cfg.T,
-                                       cfg.fire_start, cfg.inf_time, y, s));
+                                       cfg.fire_start, cfg.inf_time, y, s, fused_pred, m->net.readout));
+            readout_done = fused_pred != nullptr;
         } else {
             const bool fc = ly.d.kind == VDT_FC;
             // small fan-in: the integrator reads the spike map itself (no
@@ -539,7 +546,7 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
             if (z == c->act[ai]) ai = (ai + 1) % 3;
         }
     }
-    if (d_pred)
+    if (d_pred && !readout_done)
         VDT_CUDA(launch_readout(x, B, m->n_classes, m->net.readout, cfg.inf_time, d_pred, s));
     if (c->profiling) c->prof_batches++;
     return VDT_OK;

@@ -149,9 +149,11 @@ cudaError_t launch_encode(const float* px, float* out, long long n, int encoder,
                           float td, int T, float inf_time, cudaStream_t s);
 cudaError_t launch_pool_min(const float* in, float* out, int B, int H_in, int W_in, int C,
                             float inf_time, cudaStream_t s);
+// pred (may be null): the readout (VDT_READ_* mode) of the outputs, fused in
 cudaError_t launch_layer_vmem(const float* in, const float* W, const float* bias,
                               const float* lut_decay, int B, int C_in, int C_out, int T,
-                              float tfs, float inf_time, float* out, cudaStream_t s);
+                              float tfs, float inf_time, float* out, cudaStream_t s,
+                              int32_t* pred = nullptr, int readout = VDT_READ_ARGMAX);
 cudaError_t launch_readout(const float* out, int B, int K, int mode, float inf_time,
                            int32_t* pred, cudaStream_t s);
 
