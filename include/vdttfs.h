@@ -380,9 +380,12 @@ size_t vdt_noalloc_scratch_bytes(void);
    VDT_NOALLOC_SCRATCH_BYTES per GPU.  A layer whose lists need more
    (n_cols*(NC+1) + 2*n_cols*C_in 4-byte words, each of the three parts rounded
    up to 256 bytes; n_cols = B*H_in*W_in, or B for is_fc) returns
-   VDT_ERR_CAPACITY and launches nothing.  The first call on each device looks
-   the array's address up (with that device current) and should precede any
-   stream capture.  Calls on one device share the array, so calls that can
+   VDT_ERR_CAPACITY and launches nothing: 54 maps of 32x32x64 fit at T=80,
+   delta=4 (58 at delta=8), one 224x224x64 map at delta >= 4.  The first
+   call on each device looks the array's address up (with that device
+   current) and should precede any stream capture; the address is cached per
+   device and CUDA context, so a call after cudaDeviceReset looks it up
+   again.  Calls on one device share the array, so calls that can
    overlap on the GPU (unordered streams or threads) race; order them.
    Nothing in the array needs to start zeroed. */
 int vdt_conv_layer_noalloc(const float* d_in, int tb_mode, const float* d_kernel,
