@@ -209,18 +209,19 @@ def launches_per_step(net, kernels, pixels=True):
 # ------------------------------------------------------------------ parity --
 def stored_parity(config, out, pred, B):
     """The outputs / predictions of a step against the stored expected ones
-    of this configuration's rank-0 batch (same batch size only)."""
+    of this configuration's rank-0 batch: the configuration's own batch, or
+    (strong scaling) rank 0's share of it, stored as "<config>@<B>"."""
     import hashlib
     try:
         g = np.load(PARITY_FILE)
-        want_B = int(g[f"{config}_batch"])
     except Exception as e:
-        return {"checked": False, "why": f"no stored outputs for {config}: {e}"}
-    if want_B != B:
-        return {"checked": False, "why": f"stored outputs are for batch {want_B}, this rank runs {B}"}
+        return {"checked": False, "why": f"no stored outputs: {e}"}
+    key = config if f"{config}_batch" in g.files and int(g[f"{config}_batch"]) == B else f"{config}@{B}"
+    if f"{key}_batch" not in g.files:
+        return {"checked": False, "why": f"no stored outputs for {config} at batch {B}"}
     out = np.ascontiguousarray(out, np.float32)
-    digest_ok = hashlib.sha256(out.tobytes()).hexdigest() == str(g[f"{config}_out_sha256"])
-    bad_pred = int(np.sum(np.asarray(pred, np.int32) != g[f"{config}_pred"].astype(np.int32)))
+    digest_ok = hashlib.sha256(out.tobytes()).hexdigest() == str(g[f"{key}_out_sha256"])
+    bad_pred = int(np.sum(np.asarray(pred, np.int32) != g[f"{key}_pred"].astype(np.int32)))
     return {"checked": True,
             "against": "expected outputs of this batch (oracle pinned to the reference's kernels), "
                        "tests/golden/bench_parity.npz",

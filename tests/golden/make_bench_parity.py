@@ -6,8 +6,11 @@ configuration's batch per GPU at one GPU) is run through the CPU oracle
 (oracle/vdt_oracle.c, pinned bit for bit to the reference's own kernels by
 tests/golden/*.npz and tests/test_golden.py; the engine is checked against
 the reference kernels at these exact batches by tests/test_gpu_bench_configs.py).
-Stored per configuration: the predictions and the SHA-256 of the output
-values' bytes (float32, [batch, classes]).  CPU only, about two minutes.
+For the strong-scaling configuration (LeNet-5 C2: 65,536 images over the
+GPUs) also rank 0's batch at 2, 4 and 8 GPUs (65,536 / N images of stream 0),
+stored under "<config>@<batch>".  Stored per batch: the predictions and the
+SHA-256 of the output values' bytes (float32, [batch, classes]).  CPU only,
+about three minutes.
 
 Usage: python tests/golden/make_bench_parity.py [OUT_FILE]
 """
@@ -33,11 +36,13 @@ def digest(out) -> str:
     return hashlib.sha256(np.ascontiguousarray(out, np.float32).tobytes()).hexdigest()
 
 
-def expected(config: str):
+def expected(config: str, B: int = 0):
     """(outputs [B, classes], predictions [B]) of a bench configuration's
-    rank-0 batch at one GPU, from the oracle."""
+    rank-0 batch (the configuration's batch at one GPU, or B images), from
+    the oracle."""
     import bench
-    netname, cfg_id, B, zf, _ = bench.CONFIGS[config]
+    netname, cfg_id, B0, zf, _ = bench.CONFIGS[config]
+    B = B or B0
     if netname in ("dvs", "dvs_ref"):
         spec = nets.dvs() if netname == "dvs" else nets.dvs_ref()
         r = O.run_dvs(spec, synth.dvs_weights(spec, cfg_id), synth.dvs_frames(cfg_id, B, spec, stream=0))
@@ -51,12 +56,15 @@ def expected(config: str):
 def main():
     out_file = sys.argv[1] if len(sys.argv) > 1 else DEFAULT_OUT
     d = {}
-    for config in ("vgg16", "lenet5_b1024", "lenet5", "dvs", "dvs_ref"):
-        out, pred = expected(config)
-        d[f"{config}_batch"] = np.int64(pred.size)
-        d[f"{config}_out_sha256"] = np.array(digest(out))
-        d[f"{config}_pred"] = pred.astype(np.int8)
-        print(config, pred.size, digest(out)[:16], np.bincount(pred + 1)[:12].tolist(), flush=True)
+    cases = [(c, 0) for c in ("vgg16", "lenet5_b1024", "lenet5", "dvs", "dvs_ref")]
+    cases += [("lenet5", 65536 // n) for n in (2, 4, 8)]
+    for config, B in cases:
+        key = config if B == 0 else f"{config}@{B}"
+        out, pred = expected(config, B)
+        d[f"{key}_batch"] = np.int64(pred.size)
+        d[f"{key}_out_sha256"] = np.array(digest(out))
+        d[f"{key}_pred"] = pred.astype(np.int8)
+        print(key, pred.size, digest(out)[:16], np.bincount(pred + 1)[:12].tolist(), flush=True)
     np.savez_compressed(out_file, **d)
     print(out_file, os.path.getsize(out_file))
 
