@@ -73,7 +73,7 @@ VGG16_DENSE_MACS = 313_725_952      # dense multiply-accumulates of one 3x32x32 
 # dram__bytes_write.sum; command in the kernel's summary under profiles/),
 # keyed by (workload, layer), with the commit of the build it measured.
 DOMINANT_TRAFFIC = {
-    ("vgg16", 1): (67_331_840 + 32_903_424, "k_dense conv1_2 at B=256, build b2a7e84"),
+    ("vgg16", 1): (67_471_360 + 33_091_328, "k_dense conv1_2 at B=256, kernels of build 8509f45"),
 }
 
 
@@ -91,6 +91,8 @@ def parse():
                     help="time the reference's vdttfs_cuda and step-by-step programs only")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (small cases for profiling; not a bench line)")
+    ap.add_argument("--eager-once", action="store_true",
+                    help="one eager batch (graphs off, one sub-batch, no counting) for a profiler; no bench line")
     return ap.parse_args()
 
 
@@ -750,7 +752,7 @@ def run_dvs_engine(a):
                                   "hbm_gbs": round(alg / (kern_ms / 1e3) / 1e9, 1),
                                   "hbm_frac": round(alg / (kern_ms / 1e3) / 1e9 / peak, 4),
                                   "stage_ms": stage_ms}},
-            "gpu_launches": 13 * a.steps,
+            "gpu_launches": 11 * a.steps,      # conv1, conv2, pool1, conv3, pool2, 3 for FC1, 2 for FC2, readout
             "clocks": clk,
         }
         if world == 1 and not a.no_ref_cuda and not a.batch:
@@ -942,11 +944,31 @@ def run_baselines(a):
     return res
 
 
+def run_eager_once(a):
+    """One batch of the configuration through the engine without graphs or
+    sub-batches, each layer's launches in layer order: the program a
+    profiler captures single launches of (ncu -k / -s / -c)."""
+    import torch
+    from vdttfs import engine as E, nets, synth
+    netname, cfg_id, Bcfg, zf, _ = CONFIGS[a.config]
+    net = nets.NETS[netname]()
+    B = a.batch or Bcfg
+    m = E.Model(net, synth.kaiming_layers(net, cfg_id), lut_source=E.LUT_HOST_LIBM)
+    ctx = E.Context(m, B, graphs=False)
+    x = torch.from_numpy(synth.images(cfg_id, B, net.in_h, net.in_w, net.in_c, zf, stream=0)).cuda()
+    out, pred = ctx.infer(x, pixels=True)
+    torch.cuda.synchronize()
+    print("eager batch", a.config, B, ctx.layer_kernels(), flush=True)
+    return None
+
+
 def main():
     a = parse()
     if a.warmup < 3:
         a.warmup = 3
-    if a.baselines:
+    if a.eager_once:
+        res = run_eager_once(a)
+    elif a.baselines:
         res = run_baselines(a)
     elif a.config == "vgg16_sweep":
         res = run_sweep(a)
