@@ -51,3 +51,14 @@ def test_dvs_frames_and_int_labels(tmp_path):
     np.eye(spec.classes, dtype="<i4")[lab].tofile(tmp_path / "train_labels.bin")
     assert np.array_equal(assets.load_dvs_frames(str(tmp_path / "train_data.bin"), 2, spec), fr)
     assert np.array_equal(assets.load_onehot(str(tmp_path / "train_labels.bin"), 2, spec.classes, "<i4"), lab)
+
+
+def test_network_output_size_is_the_last_map_flattened():
+    """n_classes: an FC last layer's outputs; a conv last layer's whole map,
+    after its pool when it has one."""
+    from vdttfs import nets
+    assert nets.vgg16().n_classes == 10 and nets.lenet5().n_classes == 10
+    c = nets._conv
+    assert nets.NetSpec("a", 7, 9, 3, (c(3, 8, 3, nets.PAD_SAME),)).n_classes == 7 * 9 * 8
+    assert nets.NetSpec("b", 7, 9, 3, (c(3, 8, 3, nets.PAD_SAME, True),)).n_classes == 3 * 4 * 8
+    assert nets.NetSpec("c", 7, 9, 3, (c(3, 8, 3, nets.PAD_VALID),)).n_classes == 5 * 7 * 8

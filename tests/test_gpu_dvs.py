@@ -297,3 +297,32 @@ def test_dvs_net_profiling_and_unsupported_calls(dev):
         assert ei.value.status == 5
     ctx.close()
     net.close()
+
+
+def test_dvs_net_sizes_capacity_and_long_blob(O, dev):
+    """The task-3 model reports its seven stages and classes; a blob longer
+    than the network (the reference reads a fixed-size file) loads the same
+    weights; batches of 1 and up to the context's maximum run, and a larger
+    one is refused before any launch."""
+    import ctypes as C
+    import torch
+    from vdttfs import assets, dvs, engine as E, nets, synth
+    from vdttfs._lib import lib
+    spec = nets.dvs_ref()
+    wts = synth.dvs_weights(spec, 4)
+    blob = assets.write_dvs_flat(wts, spec)
+    net = dvs.DvsNet(spec, blob + bytes(4 * 3456))           # 1,292,032 floats, as the reference's file
+    nl, nc, wb = C.c_int(), C.c_int(), C.c_size_t()
+    assert lib().vdt_model_info(net.h, C.byref(nl), C.byref(nc), C.byref(wb)) == 0
+    assert (nl.value, nc.value, wb.value) == (7, spec.classes, len(blob))
+    ctx = net.context(3)
+    frames = synth.dvs_frames(4, 3, spec, stream=70)
+    ref = O.run_dvs(spec, wts, frames)
+    for B in (1, 3):
+        out, pred = ctx.infer(torch.from_numpy(frames[:B]).to(dev))
+        assert bits_equal(_np(out), ref["out"][:B]) and np.array_equal(_np(pred), ref["pred"][:B])
+    with pytest.raises(E.VdtError) as ei:
+        ctx.infer(torch.from_numpy(synth.dvs_frames(4, 4, spec, stream=71)).to(dev))
+    assert ei.value.status == 6                               # VDT_ERR_CAPACITY
+    ctx.close()
+    net.close()

@@ -146,3 +146,29 @@ def test_readout_fused_into_the_membrane_layer(O, dev, readout):
     assert np.array_equal(_np(pred), O.readout(_np(out), B, 40, readout))
     ctx.close()
     m.close()
+
+
+def test_unpooled_conv_last_layer_output_is_the_whole_map(O, dev):
+    """A network ending in a conv layer without a pool outputs that layer's
+    whole first-spike map, flattened ([B, H * W * C]), on every path."""
+    from vdttfs import engine as E, nets, synth
+    net = nets.NetSpec("convout", 6, 5, 4, (nets._conv(4, 24, 3, nets.PAD_SAME),), T=40, delta=4, tfs=40.0,
+                       lut_mode=nets.LUT_BY_TIN, decay_len=41, readout=nets.READ_ARGMIN_FIRST,
+                       tc_in=34.75016403198242, encoder=nets.ENC_LINEAR)
+    assert net.n_classes == 6 * 5 * 24
+    layers = synth.kaiming_layers(net, 1, gains=[1.6])
+    B = 7
+    spikes = O.encode_linear(synth.images(1, B, 6, 5, 4, 0.3, stream=37), net.T)
+    ref = O.run_net(net, layers, spikes)
+    m = E.Model(net, layers, lut_source=E.LUT_HOST_LIBM)
+    assert m.n_classes == net.n_classes
+    ctx = E.Context(m, B)
+    for kernel in (DENSE, SORTED, CHUNK):
+        ctx.set_layer_kernel(0, kernel)
+        out, pred = ctx.infer(_t(spikes))
+        assert _np(out).shape == (B, net.n_classes)
+        assert bits_equal(_np(out), ref["out"]) and np.array_equal(_np(pred), ref["pred"]), f"kernel {kernel}"
+        o2, p2 = ctx.infer_host(spikes)
+        assert bits_equal(o2, ref["out"]) and np.array_equal(p2, ref["pred"])
+    ctx.close()
+    m.close()

@@ -21,7 +21,9 @@
 //      O(log T) (Lanes::close_empty), input-free chunks cost nothing.
 //   The warp stops once all its neurons fired (later chunks are never
 //   fetched).  A chunk with more events than the per-warp record buffer is
-//   integrated in arrival-order segments into per-slot registers instead.
+//   sorted and streamed in segments of half a buffer; each slot's partial
+//   sum carries over between segments in shared memory (the chain order is
+//   the same), and the chunk's steps close after its last segment.
 #include <type_traits>
 
 #include "lanes.h"
@@ -32,7 +34,6 @@ namespace {
 
 constexpr int SWARPS = 4;    // warps per CTA
 constexpr int SEG = 512;     // records per warp buffer
-constexpr int SUB = 4;       // weight rows in flight per batch (oversize chunks)
 constexpr int FS = 8;        // records per streamed block
 constexpr int ROW_MASK = 0xffffff;      // decoded record.x: row | slot << 24
 
@@ -43,42 +44,16 @@ __host__ __device__ inline int sorted_words(int ntaps, int OS) {
     return 2 * SEG * 2 + 2 * 96 + 64 + 3 * 32 + 2 * 64 + ((ntaps * OS + 3) & ~3);
 }
 
-// delta[S] += the run [a, b) of slot-sorted records (oversize chunks)
-template <int DELTA, int V, int S>
-__device__ __forceinline__ void stream_slot(float (&d)[DELTA][V], const int2* rec, int a, int b,
-                                            const float* Wl, int C_out) {
-    int k = a;
-    for (; k + SUB <= b; k += SUB) {
-        int2 e[SUB];
-        float w[SUB][V];
-#pragma unroll
-        for (int u = 0; u < SUB; ++u) e[u] = rec[k + u];
-#pragma unroll
-        for (int u = 0; u < SUB; ++u) load_row<V>(Wl + (unsigned)e[u].x, w[u]);
-#pragma unroll
-        for (int u = 0; u < SUB; ++u) {
-            const float lv = __int_as_float(e[u].y);
-#pragma unroll
-            for (int v = 0; v < V; ++v) d[S][v] = fmaf(w[u][v], lv, d[S][v]);
-        }
-    }
-    for (; k < b; ++k) {
-        const int2 e = rec[k];
-        float w[V];
-        load_row<V>(Wl + (unsigned)e.x, w);
-        const float lv = __int_as_float(e.y);
-#pragma unroll
-        for (int v = 0; v < V; ++v) d[S][v] = fmaf(w[v], lv, d[S][v]);
-    }
-}
-
-template <int DELTA, int V, int S = 0>
-__device__ __forceinline__ void stream_all(float (&d)[DELTA][V], const int2* rec, const int* start,
-                                           const float* Wl, int C_out) {
-    if constexpr (S < DELTA) {
-        const int a = start[S], b = start[S + 1];
-        if (a < b) stream_slot<DELTA, V, S>(d, rec, a, b, Wl, C_out);
-        stream_all<DELTA, V, S + 1>(d, rec, start, Wl, C_out);
+template <int V>
+__device__ __forceinline__ void load_row_shared(const float* p, float (&w)[V]) {
+    if constexpr (V == 1) {
+        w[0] = *p;
+    } else if constexpr (V == 2) {
+        const float2 v = *reinterpret_cast<const float2*>(p);
+        w[0] = v.x; w[1] = v.y;
+    } else {
+        const float4 v = *reinterpret_cast<const float4*>(p);
+        w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
     }
 }
 
@@ -194,58 +169,55 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
         if (!__any_sync(FULL_MASK, nu.any())) break;
         if (lane < ntaps) { s_pre[lane] = inc - cnt; s_st[lane] = st; }
         __syncwarp();
-        const bool fits = total <= SEG;
-        float d[DELTA][V];                                   // oversize chunks only
-        if (!fits) {
-#pragma unroll
-            for (int i = 0; i < DELTA; ++i)
-#pragma unroll
-                for (int v = 0; v < V; ++v) d[i][v] = 0.0f;
-        }
-        for (int s0 = 0; s0 < total; s0 += SEG) {
-            const int segn = min(SEG, total - s0);
-            for (int i = lane; i < DELTA; i += 32) s_cnt[i] = 0;
+        // decode of the chunk's event pidx (tap order, then bucket order):
+        // its slot and record {weight row (+ slot << 24), LUT value}
+        auto decode = [&](int pidx, int& slot) -> int2 {
+            int lo = 0, hi = ntaps - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (s_pre[mid] <= pidx) lo = mid; else hi = mid - 1;
+            }
+            const long long at = s_cbase[lo] + s_st[lo] + (pidx - s_pre[lo]);
+            const int ci = __ldg(p.cin + at);
+            const float t = __ldg(p.tin + at);
+            float lv = 1.0f;                                 // CuLIF: in[t] += w exactly
+            int tb;
+            if constexpr (CULIF) {
+                tb = (int)t;
+            } else {
+                tb = (int)floorf(t - p.tfs);
+                if (tb < 0) tb = 0;
+                int ti;
+                if (p.lut_mode == VDT_LUT_BY_TB) {
+                    ti = tb;
+                } else {
+                    ti = (int)t;
+                    ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
+                }
+                lv = s_decay[ti];
+            }
+            slot = tb - base;
+            return make_int2((s_wrow[lo] + ci) | (slot << 24), __float_as_int(lv));
+        };
+        // the chunk's events [s0, s0 + n) whose slot is in [p0, p0 + nb),
+        // into s_rec grouped by slot (chain order kept inside each slot):
+        // decode into dec + a per-slot histogram (shared-memory atomics),
+        // slot offsets by a warp scan (s_start = starts, then the end), the
+        // stable scatter (rank = popc(group & lanemask_lt))
+        auto sort_slots = [&](int2* dec, int s0, int n, int p0, int nb) {
+            for (int i = lane; i < nb; i += 32) s_cnt[i] = 0;
             __syncwarp();
-            // 1. decode + per-slot histogram (shared-memory atomics)
-            for (int w0 = 0; w0 < segn; w0 += 32) {
+            for (int w0 = 0; w0 < n; w0 += 32) {
                 const int q = w0 + lane;
                 int slot = -1;
-                if (q < segn) {
-                    const int pidx = s0 + q;
-                    int lo = 0, hi = ntaps - 1;
-                    while (lo < hi) {
-                        const int mid = (lo + hi + 1) >> 1;
-                        if (s_pre[mid] <= pidx) lo = mid; else hi = mid - 1;
-                    }
-                    const long long at = s_cbase[lo] + s_st[lo] + (pidx - s_pre[lo]);
-                    const int ci = __ldg(p.cin + at);
-                    const float t = __ldg(p.tin + at);
-                    float lv = 1.0f;                         // CuLIF: in[t] += w exactly
-                    int tb;
-                    if constexpr (CULIF) {
-                        tb = (int)t;
-                    } else {
-                        tb = (int)floorf(t - p.tfs);
-                        if (tb < 0) tb = 0;
-                        int ti;
-                        if (p.lut_mode == VDT_LUT_BY_TB) {
-                            ti = tb;
-                        } else {
-                            ti = (int)t;
-                            ti = ti < 0 ? 0 : (ti > p.T ? p.T : ti);
-                        }
-                        lv = s_decay[ti];
-                    }
-                    slot = tb - base;
-                    s_tmp[q] = make_int2((s_wrow[lo] + ci) | (slot << 24), __float_as_int(lv));
-                }
-                if (slot >= 0) atomicAdd(&s_cnt[slot], 1);   // counts only: order is free
+                if (q < n) dec[q] = decode(s0 + q, slot);
+                slot -= p0;
+                if (slot >= 0 && slot < nb) atomicAdd(&s_cnt[slot], 1);   // counts only: order is free
             }
             __syncwarp();
-            // 2. slot offsets, the stable scatter into slot order
-            for (int c = 0; c < DELTA; c += 32) {
+            for (int c = 0; c < nb; c += 32) {
                 const int i = c + lane;
-                const int v = i < DELTA ? s_cnt[i] : 0;
+                const int v = i < nb ? s_cnt[i] : 0;
                 int x = v;
 #pragma unroll
                 for (int dd = 1; dd < 32; dd <<= 1) {
@@ -253,17 +225,18 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
                     if (lane >= dd) x += u;
                 }
                 const int prev = c == 0 ? 0 : s_start[c];
-                if (i < DELTA) { s_start[i] = prev + x - v; s_cnt[i] = prev + x - v; }
-                if (lane == 31) s_start[min(c + 32, DELTA)] = prev + x;
+                if (i < nb) { s_start[i] = prev + x - v; s_cnt[i] = prev + x - v; }
+                if (lane == 31) s_start[min(c + 32, nb)] = prev + x;
                 __syncwarp();
             }
-            for (int w0 = 0; w0 < segn; w0 += 32) {
+            for (int w0 = 0; w0 < n; w0 += 32) {
                 const int q = w0 + lane;
                 int slot = -1;
                 int2 e = make_int2(0, 0);
-                if (q < segn) {
-                    e = s_tmp[q];
-                    slot = e.x >> 24;
+                if (q < n) {
+                    e = dec[q];
+                    slot = (e.x >> 24) - p0;
+                    if (slot >= nb) slot = -1;
                     e.x = (e.x & ROW_MASK) * p.C_out;        // element offset of the weight row
                 }
                 const unsigned g = __match_any_sync(FULL_MASK, slot);
@@ -276,36 +249,63 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
                 }
                 __syncwarp();
             }
-            if (fits) {
-                // 3. the chunk's non-empty slots as runs, then one streamed pass
-                const int nruns = compact_runs(s_start + 1, DELTA, base, s_runs);
-                if constexpr (CULIF) done = !stream_runs<V, FS>(nu, s_rec, 0, s_runs, nruns, Wl, next_t, cc);
-                else done = !stream_runs<V, FS>(nu, s_rec, 0, s_runs, nruns, Wl, next_t, tt);
+        };
+        if (total <= SEG) {
+            sort_slots(s_tmp, 0, total, 0, DELTA);
+            // the chunk's non-empty slots as runs, then one streamed pass
+            const int nruns = compact_runs(s_start + 1, DELTA, base, s_runs);
+            if constexpr (CULIF) {
+                done = !stream_runs<V, FS>(nu, s_rec, 0, s_runs, nruns, Wl, next_t, cc);
+                if (!done) {
+                    nu.close_empty(next_t, base + DELTA, cc);    // the chunk's remaining steps
+                    next_t = base + DELTA;
+                    done = !__any_sync(FULL_MASK, nu.any());
+                }
             } else {
-                stream_all<DELTA, V>(d, s_rec, s_start, Wl, p.C_out);
+                done = !stream_runs<V, FS>(nu, s_rec, 0, s_runs, nruns, Wl, next_t, tt);
             }
             __syncwarp();
-        }
-        if (!fits) {
-            // per-slot chains complete: close the chunk's steps in order
-            // (the CuLIF scan has no t < T guard, t3:137-141)
+        } else {
+            // more events than the record buffer: segments of SEG / 2 events,
+            // each sorted by slot like a chunk that fits (decoded into the
+            // upper half of s_rec, scattered into the lower half); every
+            // slot's partial sum carries over between segments in the s_tmp
+            // words, so each slot's chain keeps the event order.  Then the
+            // chunk's steps close in order (the CuLIF scan has no t < T
+            // guard, t3:137-141).
+            constexpr int HS = SEG / 2;
+            constexpr int SPP = DELTA * V <= 32 ? DELTA : 32 / V;  // slots per pass: their sums fill s_tmp
+            float* s_acc = reinterpret_cast<float*>(s_tmp) + lane * V;   // slot p0 + i at + i * 32 * V
+            int2* s_dec = s_rec + HS;
+            const unsigned sa_rec = (unsigned)__cvta_generic_to_shared(s_rec);
+            const float zero[V] = {};
+            for (int p0 = 0; p0 < DELTA; p0 += SPP) {
 #pragma unroll
-            for (int i = 0; i < DELTA; ++i) {
-                if (CULIF || base + i < p.T) {
-#pragma unroll
-                    for (int v = 0; v < V; ++v) nu.acc[v] = d[i][v];
-                    if constexpr (CULIF) nu.close_step_bf(base + i, cc);
-                    else nu.close_step(base + i, tt);
+                for (int i = 0; i < SPP; ++i) store_res<V>(s_acc + i * 32 * V, zero);
+                for (int s0 = 0; s0 < total; s0 += HS) {
+                    const int segn = min(HS, total - s0);
+                    sort_slots(s_dec, s0, segn, p0, SPP);
+                    const int nruns = compact_runs(s_start + 1, SPP, 0, s_runs);
+                    int k = 0;
+                    for (int j = 0; j < nruns; ++j) {
+                        const int2 rn = s_runs[j];
+                        load_row_shared<V>(s_acc + rn.y * 32 * V, nu.acc);
+                        stream_run_records<V, FS>(nu, sa_rec, k, rn.x, Wl);
+                        store_res<V>(s_acc + rn.y * 32 * V, nu.acc);
+                        k = rn.x;
+                    }
+                    __syncwarp();
                 }
+                for (int i = 0; i < SPP; ++i) {
+                    if (!CULIF && base + p0 + i >= p.T) break;
+                    load_row_shared<V>(s_acc + i * 32 * V, nu.acc);
+                    if constexpr (CULIF) nu.close_step_bf(base + p0 + i, cc);
+                    else nu.close_step(base + p0 + i, tt);
+                }
+                __syncwarp();
             }
             next_t = CULIF ? base + DELTA : min(p.T, base + DELTA);
             done = !__any_sync(FULL_MASK, nu.any());
-        } else if constexpr (CULIF) {
-            if (!done) {
-                nu.close_empty(next_t, base + DELTA, cc);    // the chunk's remaining steps
-                next_t = base + DELTA;
-                done = !__any_sync(FULL_MASK, nu.any());
-            }
         }
     }
     if constexpr (!CULIF) {
@@ -339,10 +339,10 @@ cudaError_t launch_sorted_dv(const IntegParams& p, cudaStream_t s, int n_warps, 
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
     const size_t smem = (size_t)SWARPS * sorted_words(ntaps, p.NC + 1) * sizeof(int) +
                         (CULIF ? 0 : (size_t)(p.decay_len + 2 * p.T) * sizeof(float));
-    // registers: the streamed block (FS weight rows + records) plus lane
-    // state; the rare oversize-chunk path may spill
-    constexpr int REGS = FS * V + 2 * FS + 4 * V + 60;
-    constexpr int MINB = (65536 / (SWARPS * 32 * REGS)) > 8 ? 8 : (65536 / (SWARPS * 32 * REGS));
+    // occupancy: 5 CTAs of 4 warps per SM, what the record buffers allow
+    // (about 43 KB of shared memory per CTA for 3x3 taps); the register cap
+    // that goes with it (102) costs V = 4 a few bytes of spill
+    constexpr int MINB = 5;
     auto kern = k_sorted<DELTA, V, MINB, CULIF>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
