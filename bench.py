@@ -454,7 +454,8 @@ def run_engine(a):
                     "h2d_bytes_per_step": int(img.nbytes),
                     "d2h_bytes_per_step": int(B * net.n_classes * 4 + B * 4),
                     "api": "vdt_infer_host_batches (pipelined, batch > L2)" if pipelined
-                    else "vdt_infer_host per step, L2 flushed between steps"},
+                    else "vdt_infer_host per step, L2 flushed between steps",
+                    "step_ms": step_spread(e_times, a.steps)},
             "parity": stored_parity(a.config, step_out, step_pred, B) if not a.batch else {"checked": False},
             "roofline": {
                 "bound": "hbm", "achieved": round(dom_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
@@ -510,6 +511,16 @@ def run_engine(a):
 
 
 # --------------------------------------------------------------- CPU legs --
+def step_spread(times_ms, steps):
+    """min / median / max of the per-step times (one pipelined call over all
+    steps gives only its mean)."""
+    t = np.asarray(times_ms, np.float64)
+    if t.size == 1 and steps > 1:
+        return {"mean": round(float(t[0]) / steps, 4)}
+    return {"min": round(float(t.min()), 4), "median": round(float(np.median(t)), 4),
+            "max": round(float(t.max()), 4)}
+
+
 def cpu_baseline(net, layers, img, cfg_id, budget_s=20.0):
     """Oracle port on a bounded sample: grow the sample until one pass takes
     ~budget_s / 4, then time passes until ~budget_s elapsed."""
@@ -741,6 +752,7 @@ def run_dvs_engine(a):
                     "d2h_bytes_per_step": int(B * spec.classes * 4 + B * 4),
                     "api": "vdt_infer_host_batches (pipelined, frames > L2)" if big
                     else "vdt_infer_host per step, L2 flushed between steps",
+                    "step_ms": step_spread(e_times, a.steps),
                     "parity_vs_device_step": live_parity(e2e_out, e2e_pred, step_out, step_pred)["result"]},
             "parity": stored_parity(a.config, step_out, step_pred, B) if not a.batch else {"checked": False},
             "roofline": {"bound": "hbm", "achieved": round(conv1_gbs, 1), "peak": peak, "unit": "GB/s",

@@ -223,7 +223,11 @@ int vdt_ctx_set_sub_batches(vdt_ctx* c, int n);
 int vdt_infer(vdt_ctx* c, const float* d_input, int input_is_pixels, int batch,
               float* d_out, int32_t* d_pred);
 /* Same, end to end from host buffers: H2D copy of the input, the network,
-   D2H copy of outputs; synchronous. */
+   D2H copy of outputs; synchronous.  With sub-batches (and graphs on) each
+   part runs as its own graph on its own stream as soon as its share of the
+   input has landed (the parts' inputs cross in order on a copy stream), and
+   copies its outputs back on that stream: part 0 computes while part 1's
+   input is still crossing.  h_pred may be NULL. */
 int vdt_infer_host(vdt_ctx* c, const float* h_input, int input_is_pixels, int batch,
                    float* h_out, int32_t* h_pred);
 /* n_batches batches of `batch` images each, end to end from host buffers,

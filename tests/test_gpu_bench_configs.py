@@ -89,6 +89,15 @@ def test_bench_path_matches_reference_program(O, dev, name, task, cfg_id, B, zf)
     n_bad = int(np.sum(out.view(np.int32) != r_out.view(np.int32)))
     assert n_bad == 0, f"{n_bad} of {out.size} output values differ from the reference program"
     assert np.array_equal(pred, r_pred), f"{int(np.sum(pred != r_pred))} predictions differ"
+    # bench.py's end-to-end call: pinned host pixels in, host outputs back,
+    # the sub-batches' copies overlapped with each other's compute
+    import torch
+    h_in = torch.from_numpy(img).pin_memory()
+    h_out = torch.empty(out.shape, dtype=torch.float32).pin_memory()
+    h_pred = torch.empty(pred.shape, dtype=torch.int32).pin_memory()
+    for _ in range(2):
+        ctx.infer_host(h_in, pixels=True, out=h_out, pred=h_pred)
+        assert bits_equal(h_out.numpy(), r_out) and np.array_equal(h_pred.numpy(), r_pred), "vdt_infer_host"
     fired = np.mean(r_out < net.inf_time) if net.readout != 2 else 1.0
     assert fired > 0.0, "no output neuron fired: the case tests nothing"
     ctx.close()

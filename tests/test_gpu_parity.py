@@ -396,9 +396,10 @@ def test_infer_host_batches_pipelined(O, dev, graphs):
 @pytest.mark.parametrize("name,B", [("vgg16", 5), ("lenet5", 33), ("vgg16", 1)])
 def test_sub_batches_change_nothing(O, dev, name, B):
     """vdt_ctx_set_sub_batches(n) (each batch as n parts on n streams, graph
-    and eager paths, device and pipelined host entry points) gives the whole
-    batch's outputs and predictions bit for bit, for n = 2..4 and batches
-    that do not divide evenly (or are smaller than n)."""
+    and eager paths, device, host and pipelined host entry points) gives the
+    whole batch's outputs and predictions bit for bit, for n = 2..4 and
+    batches that do not divide evenly (or are smaller than n).  The host
+    call runs one graph per part, each part's copies on its own stream."""
     from vdttfs import engine as E
     net, layers, img = _net_case(name, B, 3 if name == "vgg16" else 1, 0.0 if name == "vgg16" else 0.8)
     spikes = O.encode_linear(img, net.T)
@@ -412,6 +413,13 @@ def test_sub_batches_change_nothing(O, dev, name, B):
             out, pred = ctx.infer(_t(spikes, dev))
             _sync()
             assert bits_equal(_np(out), ref["out"]) and np.array_equal(_np(pred), ref["pred"]), f"n={n} graphs={graphs}"
+            for _ in range(2):                               # the second call reuses the parts' graphs
+                o, p = ctx.infer_host(spikes.copy())
+                assert bits_equal(o, ref["out"]) and np.array_equal(p, ref["pred"]), f"host n={n} graphs={graphs}"
+            from vdttfs._lib import lib
+            o = np.empty_like(ref["out"])
+            assert lib().vdt_infer_host(ctx.h, spikes.ctypes.data, 0, B, o.ctypes.data, None) == 0   # no predictions
+            assert bits_equal(o, ref["out"])
         outs, preds = ctx.infer_host_batches([spikes, spikes])
         assert all(bits_equal(o, ref["out"]) for o in outs) and all(np.array_equal(p, ref["pred"]) for p in preds)
     ctx.set_counting(True)                                   # counting passes run whole batches

@@ -56,10 +56,13 @@ struct vdt_model {
     vdt::DvsWeights dw{};
 };
 
+// part 0: a whole batch (its sub-batches forked and joined inside the
+// graph); part k + 1: sub-batch k alone, on its workspace (the host path)
 struct GraphKey {
-    int batch, pixels, counting, slot;
+    int batch, pixels, counting, slot, part;
     bool operator<(const GraphKey& o) const {
-        return std::tie(batch, pixels, counting, slot) < std::tie(o.batch, o.pixels, o.counting, o.slot);
+        return std::tie(batch, pixels, counting, slot, part) <
+               std::tie(o.batch, o.pixels, o.counting, o.slot, o.part);
     }
 };
 
@@ -72,12 +75,15 @@ struct vdt_ctx {
     float* in_slot = nullptr;    // [max_batch, in_elems]
     float* out_slot = nullptr;   // [max_batch, classes]
     int32_t* pred_slot = nullptr;
-    // second input/output slot, copy stream and events of the pipelined host
-    // path (vdt_infer_host_batches), made on its first call
+    // copy stream of the host paths and the per-part input events of
+    // vdt_infer_host, made on first use
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t ev_part[VDT_MAX_SUB_BATCHES] = {};
+    // second input/output slot and events of the pipelined host path
+    // (vdt_infer_host_batches), made on its first call
     float* in_slot2 = nullptr;
     float* out_slot2 = nullptr;
     int32_t* pred_slot2 = nullptr;
-    cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_h2d[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
     // sub-batches (vdt_ctx_set_sub_batches): parts 1.. of a batch run on
     // their own streams with their own activation and bucket workspaces

@@ -419,6 +419,8 @@ void ctx_free(vdt_ctx* c) {
         if (c->ev_h2d[i]) cudaEventDestroy(c->ev_h2d[i]);
         if (c->ev_done[i]) cudaEventDestroy(c->ev_done[i]);
     }
+    for (auto e : c->ev_part)
+        if (e) cudaEventDestroy(e);
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     for (auto& w : c->sub) {
         for (auto& a : w.act) cudaFree(a);
@@ -791,15 +793,13 @@ extern "C" int vdt_ctx_set_layer_kernel(vdt_ctx* c, int layer, int kernel) {
 
 // Run one batch from the ctx's input slot `slot` (0: in_slot, 1: in_slot2)
 // into the matching output slots, through a cached CUDA graph when enabled.
-static int run_slots(vdt_ctx* c, int pixels, int batch, int slot = 0) {
-    float* in = slot ? c->in_slot2 : c->in_slot;
-    float* out = slot ? c->out_slot2 : c->out_slot;
-    int32_t* pred = slot ? c->pred_slot2 : c->pred_slot;
-    if (!c->graphs || c->profiling) return enqueue_split(c, in, pixels, batch, out, pred);
-    const GraphKey key{batch, pixels, c->counting ? 1 : 0, slot};
+// The executable graph cached under key, captured on first use from what
+// enqueue_fn() enqueues on c->stream (pointed at a private capture stream
+// meanwhile: the legacy default stream can't be captured).
+template <class F>
+static int cached_graph(vdt_ctx* c, const GraphKey& key, F&& enqueue_fn, cudaGraphExec_t* ex) {
     auto it = c->cache.find(key);
     if (it == c->cache.end()) {
-        // capture on a private stream: the legacy default stream can't be captured
         cudaStream_t cap;
         VDT_CUDA(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
         cudaStream_t user = c->stream;
@@ -807,20 +807,108 @@ static int run_slots(vdt_ctx* c, int pixels, int batch, int slot = 0) {
         cudaGraph_t graph = nullptr;
         cudaError_t e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
         int st = VDT_OK;
-        if (e == cudaSuccess) st = enqueue_split(c, in, pixels, batch, out, pred);
+        if (e == cudaSuccess) st = enqueue_fn();
         cudaError_t e2 = cudaStreamEndCapture(cap, &graph);
         c->stream = user;
         cudaStreamDestroy(cap);
         if (e != cudaSuccess) return cuda_fail(e, "cudaStreamBeginCapture");
         if (st != VDT_OK) { if (graph) cudaGraphDestroy(graph); return st; }
         if (e2 != cudaSuccess) return cuda_fail(e2, "cudaStreamEndCapture");
-        cudaGraphExec_t ex;
-        e = cudaGraphInstantiate(&ex, graph, 0);
+        cudaGraphExec_t x;
+        e = cudaGraphInstantiate(&x, graph, 0);
         cudaGraphDestroy(graph);
         if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
-        it = c->cache.emplace(key, ex).first;
+        it = c->cache.emplace(key, x).first;
     }
-    VDT_CUDA(cudaGraphLaunch(it->second, c->stream));
+    *ex = it->second;
+    return VDT_OK;
+}
+
+static int run_slots(vdt_ctx* c, int pixels, int batch, int slot = 0) {
+    float* in = slot ? c->in_slot2 : c->in_slot;
+    float* out = slot ? c->out_slot2 : c->out_slot;
+    int32_t* pred = slot ? c->pred_slot2 : c->pred_slot;
+    if (!c->graphs || c->profiling) return enqueue_split(c, in, pixels, batch, out, pred);
+    cudaGraphExec_t ex = nullptr;
+    const GraphKey key{batch, pixels, c->counting ? 1 : 0, slot, 0};
+    if (int st = cached_graph(c, key, [&] { return enqueue_split(c, in, pixels, batch, out, pred); }, &ex))
+        return st;
+    VDT_CUDA(cudaGraphLaunch(ex, c->stream));
+    return VDT_OK;
+}
+
+static int ensure_copy_stream(vdt_ctx* c) {
+    if (c->copy_stream) return VDT_OK;
+    cudaStream_t cs = nullptr;
+    VDT_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+    c->copy_stream = cs;
+    return VDT_OK;
+}
+
+// One batch from host memory as its sub-batches, each overlapping the
+// others' copies: part k's input crosses on the copy stream (the parts in
+// order), its graph (part k alone, on its workspace) runs on its own stream
+// once that input has landed, and its outputs cross back on the same stream.
+// Part 0 computes while part 1's input is still crossing.  Same kernels and
+// results as the whole-batch graph.
+static int infer_host_parts(vdt_ctx* c, const float* h_input, int pixels, int batch, float* h_out,
+                            int32_t* h_pred) {
+    const vdt_model* m = c->m;
+    const int n = std::min(c->n_sub, batch);
+    if (int st = ensure_copy_stream(c)) return st;
+    for (int k = 0; k < n; ++k)
+        if (!c->ev_part[k]) VDT_CUDA(cudaEventCreateWithFlags(&c->ev_part[k], cudaEventDisableTiming));
+    const size_t in_row = m->in_elems;
+    cudaStream_t cs = c->copy_stream;
+    // the inputs may land once earlier work on the ctx stream is done with the slot
+    VDT_CUDA(cudaEventRecord(c->ev_fork, c->stream));
+    VDT_CUDA(cudaStreamWaitEvent(cs, c->ev_fork, 0));
+    int b0 = 0;
+    for (int k = 0; k < n; ++k) {
+        const int bk = batch / n + (k < batch % n ? 1 : 0);
+        VDT_CUDA(cudaMemcpyAsync(c->in_slot + (size_t)b0 * in_row, h_input + (size_t)b0 * in_row,
+                                 (size_t)bk * in_row * sizeof(float), cudaMemcpyHostToDevice, cs));
+        VDT_CUDA(cudaEventRecord(c->ev_part[k], cs));
+        b0 += bk;
+    }
+    b0 = 0;
+    for (int k = 0; k < n; ++k) {
+        const int bk = batch / n + (k < batch % n ? 1 : 0);
+        const float* in = c->in_slot + (size_t)b0 * in_row;
+        float* out = c->out_slot + (size_t)b0 * m->n_classes;
+        int32_t* pred = c->pred_slot + b0;
+        cudaStream_t sk = k == 0 ? c->stream : c->sub[k - 1].stream;
+        cudaGraphExec_t ex = nullptr;
+        const GraphKey key{bk, pixels, 0, 0, k + 1};
+        auto part = [&] {
+            if (k == 0) return enqueue(c, in, pixels, bk, out, pred, nullptr);
+            vdt_ctx::SubWs& w = c->sub[k - 1];                // this part's workspace
+            auto swap_ws = [&] {
+                for (int i = 0; i < 3; ++i) std::swap(c->act[i], w.act[i]);
+                std::swap(c->off, w.off);
+                std::swap(c->cin, w.cin);
+                std::swap(c->tin, w.tin);
+            };
+            swap_ws();
+            const int st = enqueue(c, in, pixels, bk, out, pred, nullptr);
+            swap_ws();
+            return st;
+        };
+        if (int st = cached_graph(c, key, part, &ex)) return st;
+        VDT_CUDA(cudaStreamWaitEvent(sk, c->ev_part[k], 0));
+        VDT_CUDA(cudaGraphLaunch(ex, sk));
+        if (h_out)
+            VDT_CUDA(cudaMemcpyAsync(h_out + (size_t)b0 * m->n_classes, out, (size_t)bk * m->n_classes * sizeof(float),
+                                     cudaMemcpyDeviceToHost, sk));
+        if (h_pred)
+            VDT_CUDA(cudaMemcpyAsync(h_pred + b0, pred, (size_t)bk * sizeof(int32_t), cudaMemcpyDeviceToHost, sk));
+        if (k > 0) {
+            VDT_CUDA(cudaEventRecord(c->sub[k - 1].join, sk));
+            VDT_CUDA(cudaStreamWaitEvent(c->stream, c->sub[k - 1].join, 0));
+        }
+        b0 += bk;
+    }
+    VDT_CUDA(cudaStreamSynchronize(c->stream));
     return VDT_OK;
 }
 
@@ -858,6 +946,8 @@ extern "C" int vdt_infer_host(vdt_ctx* c, const float* h_input, int input_is_pix
     if (!h_input) return fail(VDT_ERR_INVALID, "h_input is NULL");
     DeviceGuard g(c->m->device);
     const vdt_model* m = c->m;
+    if (c->graphs && !c->profiling && !c->counting && std::min(c->n_sub, batch) >= 2)
+        return infer_host_parts(c, h_input, input_is_pixels, batch, h_out, h_pred);
     const size_t in_n = (size_t)batch * m->in_elems;
     VDT_CUDA(cudaMemcpyAsync(c->in_slot, h_input, in_n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     if (c->graphs) {
@@ -875,23 +965,22 @@ extern "C" int vdt_infer_host(vdt_ctx* c, const float* h_input, int input_is_pix
     return VDT_OK;
 }
 
-// Resources of the pipelined host path, made once per ctx.
+// Resources of the pipelined host path, made once per ctx (each only if
+// missing, so a call after a failed one retries without leaking).
 static int ensure_pipeline(vdt_ctx* c) {
-    if (c->copy_stream) return VDT_OK;
     const vdt_model* m = c->m;
     const size_t in_n = (size_t)c->max_batch * m->in_elems;
-    cudaError_t e = cudaMalloc(&c->in_slot2, in_n * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&c->out_slot2, (size_t)c->max_batch * m->n_classes * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&c->pred_slot2, (size_t)c->max_batch * sizeof(int32_t));
+    cudaError_t e = cudaSuccess;
+    if (!c->in_slot2) e = cudaMalloc(&c->in_slot2, in_n * sizeof(float));
+    if (e == cudaSuccess && !c->out_slot2)
+        e = cudaMalloc(&c->out_slot2, (size_t)c->max_batch * m->n_classes * sizeof(float));
+    if (e == cudaSuccess && !c->pred_slot2) e = cudaMalloc(&c->pred_slot2, (size_t)c->max_batch * sizeof(int32_t));
     for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
-        e = cudaEventCreateWithFlags(&c->ev_h2d[i], cudaEventDisableTiming);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_done[i], cudaEventDisableTiming);
+        if (!c->ev_h2d[i]) e = cudaEventCreateWithFlags(&c->ev_h2d[i], cudaEventDisableTiming);
+        if (e == cudaSuccess && !c->ev_done[i]) e = cudaEventCreateWithFlags(&c->ev_done[i], cudaEventDisableTiming);
     }
-    cudaStream_t cs = nullptr;
-    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
     if (e != cudaSuccess) return cuda_fail(e, "pipelined host path resources");
-    c->copy_stream = cs;
-    return VDT_OK;
+    return ensure_copy_stream(c);
 }
 
 extern "C" int vdt_infer_host_batches(vdt_ctx* c, int n_batches, const float* const* h_inputs,
