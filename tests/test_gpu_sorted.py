@@ -1,12 +1,18 @@
-"""GPU: k_sorted's chunks with more events than its per-warp record buffer
-(512 records), integrated slot by slot, against the oracle bit for bit.
+"""GPU: k_sorted against the oracle bit for bit, on the paths the dense VGG-16
+workload reaches rarely or never.
 
-Every input here fires inside one k_sorted chunk (8 steps), so a pixel's
-chunk holds about 60% of its K*K*C_in inputs: 1,382 events for 3x3x256
-inputs.  Both neuron models go through that path: the LIF integrator of
-tasks 1-2 (k_conv_bucketed, t2:84-170, via a network layer forced onto
-k_sorted) and the task-3 CuLIF one (conv_bucketed_early, t3:109-143, via
-vdt_dvs_conv_bucketed at chunk width 8).
+* Chunks with more events than the record buffer (512 records), integrated
+  in sorted segments.  Every input here fires inside one k_sorted chunk (8
+  steps), so a pixel's chunk holds about 60% of its K*K*C_in inputs: 1,382
+  events for 3x3x256 inputs.  Both neuron models go through that path: the
+  LIF integrator of tasks 1-2 (k_conv_bucketed, t2:84-170, via a network
+  layer forced onto k_sorted) and the task-3 CuLIF one (conv_bucketed_early,
+  t3:109-143, via vdt_dvs_conv_bucketed at chunk width 8).
+* Teams: with 2 or 4 channel groups per pixel (C_out 256 / 512 at 4
+  channels per lane), the group warps share the pixel's sort; the output
+  maps have an odd pixel count, so the grid's last CTA holds one team of
+  two.  One case gives each channel group its own bias, so some warps of a
+  team have all fired while the others still integrate.
 """
 import numpy as np
 import pytest
@@ -29,11 +35,13 @@ def _np(t):
     return t.detach().cpu().numpy()
 
 
+@pytest.mark.parametrize("C_out", [128, 256, 512], ids=["team1", "team2", "team4"])
 @pytest.mark.parametrize("tfs,T", [(40.0, 80), (0.0, 37)], ids=["task2", "task1"])
-def test_sorted_oversize_chunks_lif(O, dev, tfs, T):
+def test_sorted_oversize_chunks_lif(O, dev, tfs, T, C_out):
     from vdttfs import engine as E, nets, synth
     task2 = tfs > 0
-    net = nets.NetSpec("big", 4, 5, 256, (nets._conv(256, 128, 3, nets.PAD_SAME), nets._fc(4 * 5 * 128, 10)),
+    H, W = 3, 5
+    net = nets.NetSpec("big", H, W, 256, (nets._conv(256, C_out, 3, nets.PAD_SAME), nets._fc(H * W * C_out, 10)),
                        T=T, delta=8, tfs=tfs, lut_mode=nets.LUT_BY_TIN if task2 else nets.LUT_BY_TB,
                        decay_len=T + 1 if task2 else T, readout=nets.READ_ARGMIN_FIRST,
                        tc_in=34.75016403198242 if task2 else 17.452274, encoder=nets.ENC_LINEAR)
@@ -41,7 +49,7 @@ def test_sorted_oversize_chunks_lif(O, dev, tfs, T):
     rng = np.random.default_rng(5)
     B = 3
     lo = tfs if task2 else 0.0                              # all events in the first k_sorted chunk (8 steps)
-    x = np.where(rng.random((B, 4, 5, 256)) < 0.6, np.floor(lo + 8 * rng.random((B, 4, 5, 256))), INF)
+    x = np.where(rng.random((B, H, W, 256)) < 0.6, np.floor(lo + 8 * rng.random((B, H, W, 256))), INF)
     x = x.astype(np.float32)
     ref = O.run_net(net, layers, x, keep=True)
     fired = np.mean(ref["maps"][0] < INF)
@@ -58,11 +66,12 @@ def test_sorted_oversize_chunks_lif(O, dev, tfs, T):
     m.close()
 
 
-def test_sorted_oversize_chunks_culif(O, dev):
+@pytest.mark.parametrize("C_out", [64, 256, 512], ids=["team1", "team2", "team4"])
+def test_sorted_oversize_chunks_culif(O, dev, C_out):
     from vdttfs import dvs, nets
     spec = nets.dvs_ref(delta=8)
     rng = np.random.default_rng(6)
-    N, C_in, C_out, H, W = 2, 160, 64, 5, 4
+    N, C_in, H, W = 1, 160, 5, 3
     x = np.where(rng.random((N, C_in, H, W)) < 0.6, np.floor(8 * rng.random((N, C_in, H, W))), INF)
     x = x.astype(np.float32)
     w = (rng.standard_normal((C_out, C_in, 3, 3)) * 0.05).astype(np.float32)
@@ -76,3 +85,39 @@ def test_sorted_oversize_chunks_culif(O, dev):
     got = _np(out)
     assert bits_equal(got, ref), f"{np.sum(got != ref)} of {ref.size} differ"
     assert 0.0 < np.mean(ref < INF) < 1.0
+
+
+@pytest.mark.parametrize("C_out", [256, 512], ids=["team2", "team4"])
+def test_team_warps_finish_at_different_times(O, dev, C_out):
+    """Each channel group of a pixel gets its own bias (+0.6 down to -0.3):
+    every neuron of group 0 fires around step 18, at 512 channels group 1
+    around step 43, the last group almost never; inputs spread over every
+    chunk.  The warps of a team then run out of live neurons at different
+    chunks; the maps must still equal the oracle's."""
+    from vdttfs import engine as E, nets, synth
+    H, W, C_in = 5, 3, 96
+    net = nets.NetSpec("teams", H, W, C_in, (nets._conv(C_in, C_out, 3, nets.PAD_SAME), nets._fc(H * W * C_out, 10)),
+                       T=80, delta=8, tfs=40.0, lut_mode=nets.LUT_BY_TIN, decay_len=81,
+                       readout=nets.READ_ARGMIN_FIRST, tc_in=34.75016403198242, encoder=nets.ENC_LINEAR)
+    layers = synth.kaiming_layers(net, 4, gains=[0.4, 1.0])
+    groups = C_out // 128
+    for g in range(groups):
+        layers[0].bias[g * 128:(g + 1) * 128] = 0.6 - 0.9 * g / (groups - 1)
+    rng = np.random.default_rng(7)
+    B = 3
+    x = np.where(rng.random((B, H, W, C_in)) < 0.5, np.floor(40.0 + 80 * rng.random((B, H, W, C_in))), INF)
+    x = x.astype(np.float32)
+    ref = O.run_net(net, layers, x, keep=True)
+    m0 = ref["maps"][0].reshape(B, H, W, C_out)
+    first = [float(np.mean(m0[..., g * 128:(g + 1) * 128] < INF)) for g in range(groups)]
+    assert first[0] > 0.9 and first[-1] < 0.5, f"fired fraction per group {first}"
+    done0 = np.mean(m0[..., :128].reshape(-1, 128).max(1) < INF)   # pixels whose group-0 warp finishes early
+    assert done0 > 0.9, done0
+    m = E.Model(net, layers, lut_source=E.LUT_HOST_LIBM)
+    ctx = E.Context(m, B)
+    ctx.set_layer_kernel(0, SORTED)
+    maps, out, pred = ctx.trace(_t(x, dev))
+    assert bits_equal(_np(maps[0]).reshape(-1), ref["maps"][0])
+    assert bits_equal(_np(out), ref["out"]) and np.array_equal(_np(pred), ref["pred"])
+    ctx.close()
+    m.close()
