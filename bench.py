@@ -413,8 +413,12 @@ def run_engine(a):
         e_ms = float(t.item())
     e2e = world * B * a.steps / (e_ms / 1e3)
 
-    # ---- roofline: per-launch CUDA events (eager profiling pass)
+    # ---- roofline: per-launch CUDA events (eager profiling pass, after one
+    # untimed eager batch: the first eager launches carry one-off costs)
     ctx.set_profiling(True)
+    with torch.cuda.stream(stream):
+        ctx.infer(x_dev, pixels=True, out=out, pred=pred)
+    stream.synchronize()
     ctx.layer_times()
     prof_steps = max(3, min(a.steps, 10))
     for _ in range(prof_steps):
@@ -716,8 +720,12 @@ def run_dvs_engine(a):
     e2e = world * B * a.steps / (e_ms / 1e3)
     e2e_out, e2e_pred = h_outs[a.steps - 1].numpy(), h_preds[a.steps - 1].numpy()
 
-    # per-stage roofline pass (profiling: CUDA events around every stage)
+    # per-stage roofline pass (profiling: CUDA events around every stage),
+    # after one untimed eager batch
     ctx.set_profiling(True)
+    with torch.cuda.stream(stream):
+        ctx.infer(x_dev, out=out, pred=pred)
+    stream.synchronize()
     ctx.layer_times()
     prof_steps = 3
     for _ in range(prof_steps):

@@ -107,7 +107,9 @@ struct vdt_ctx {
     bool graphs = true;
     bool counting = false;
     bool profiling = false;
-    int dense_max_fan = 1152;        // layers with K*K*C_in up to this use k_dense
+    // layers with K*K*C_in up to this use k_dense: its per-pixel window fits
+    // 8 CTAs per SM in shared memory (wider windows run k_sorted, which does)
+    int dense_max_fan = 576;
     std::vector<int> kernel_override;  // per layer: -1 automatic, else VDT_KERNEL_*
     std::map<GraphKey, cudaGraphExec_t> cache;
     // profiling: (layer, stage, start, stop) per timed launch, read back lazily

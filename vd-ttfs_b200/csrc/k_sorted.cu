@@ -37,10 +37,13 @@ namespace vdt {
 namespace {
 
 constexpr int SWARPS = 4;    // warps per CTA
-constexpr int SEG = 512;     // records per team buffer
 constexpr int FS = 8;        // records per streamed block
 constexpr int MAXS = 64;     // slots per chunk (DELTA <= 64)
 constexpr int ROW_MASK = 0xffffff;      // decoded record.x: row | slot << 24
+
+// records per team buffer: 256 for one warp per pixel (so that 8 CTAs fit
+// in shared memory), 512 for teams of 2 or 4 warps
+__host__ __device__ constexpr int seg_records(int G) { return G == 1 ? 256 : 512; }
 
 // shared words per team of G warps: records (arrival order + slot order,
 // int2 each), per-warp slot counts and cursors, slot starts (+ end), tap
@@ -48,6 +51,7 @@ constexpr int ROW_MASK = 0xffffff;      // decoded record.x: row | slot << 24
 // chunk's runs (int2 per slot), per-warp alive flags and the run count, and
 // every tap's chunk offsets
 __host__ __device__ inline int sorted_words(int ntaps, int OS, int G) {
+    const int SEG = seg_records(G);
     return 2 * SEG * 2 + 2 * G * MAXS + 96 + 64 + 3 * 32 + 2 * MAXS + 8 + ((ntaps * OS + 3) & ~3);
 }
 
@@ -84,6 +88,7 @@ __device__ __forceinline__ void team_sync(int team) {
 template <int DELTA, int V, int MINB, bool CULIF, int G>
 __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int n_warps, int groups) {
     static_assert(SWARPS % G == 0, "teams tile the CTA");
+    constexpr int SEG = seg_records(G);
     extern __shared__ __align__(16) int sm[];
     __shared__ int s_floor, s_mono;
     chain_release();
@@ -337,7 +342,7 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
             // event order.  Then the chunk's steps close in order (the CuLIF
             // scan has no t < T guard, t3:137-141).
             constexpr int HS = SEG / 2;
-            constexpr int SPW = 32 / (V * G) > 0 ? 32 / (V * G) : 1;
+            constexpr int SPW = 2 * SEG / (32 * V * G) > 0 ? 2 * SEG / (32 * V * G) : 1;
             constexpr int SPP = SPW < DELTA ? SPW : DELTA;  // slots per pass: the team's sums fill s_tmp
             float* s_acc = reinterpret_cast<float*>(s_tmp) + rank * SPP * V * 32 + lane * V;
             int2* s_dec = s_rec + HS;
@@ -409,7 +414,8 @@ cudaError_t launch_sorted_dvg(const IntegParams& p, cudaStream_t s, int n_warps,
     const size_t smem = (size_t)(SWARPS / G) * sorted_words(ntaps, p.NC + 1, G) * sizeof(int) +
                         (CULIF ? 0 : (size_t)(p.decay_len + 2 * p.T) * sizeof(float));
     // occupancy: 8 CTAs of 4 warps per SM (64 registers, a few bytes of
-    // spill; about 24 KB of shared memory per CTA for two teams of 3x3 taps)
+    // spill; about 24 KB of shared memory per CTA for 3x3 taps: two teams of
+    // two warps, or four single warps with half-size record buffers)
     constexpr int MINB = 8;
     auto kern = k_sorted<DELTA, V, MINB, CULIF, G>;
     if (smem > 48 * 1024) {
