@@ -154,8 +154,9 @@ struct Reader {
 
 namespace {
 // which integrator runs a layer: k_thread for narrow conv layers (a warp per
-// pixel would leave most lanes idle), k_dense (bucketing fused in) for small
-// per-pixel fan-in, else k_sorted, else the generic chunk integrator
+// pixel would leave most lanes idle), k_dense (bucketing fused in) up to
+// dense_max_fan inputs per pixel, else k_sorted, else k_dense if it takes the
+// layer, else the generic chunk integrator
 int layer_kernel(const vdt_ctx* c, int li, const vdt_time_cfg& cfg) {
     const Layer& ly = c->m->layers[li];
     if (ly.d.out == VDT_OUT_VMEM) return VDT_KERNEL_VMEM;
@@ -166,10 +167,10 @@ int layer_kernel(const vdt_ctx* c, int li, const vdt_time_cfg& cfg) {
     if (thread_supported(ly.d.k, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len) &&
         dense_supported(ly.d.k, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len))
         return VDT_KERNEL_THREAD;
-    if (fan <= c->dense_max_fan && dense_supported(ly.d.k, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len))
-        return VDT_KERNEL_DENSE;
+    const bool dense_ok = dense_supported(ly.d.k, fc, ly.C_in, ly.C_out, cfg.T, cfg.decay_len);
+    if (fan <= c->dense_max_fan && dense_ok) return VDT_KERNEL_DENSE;
     if (sorted_supported(K, fc, kSortedDelta, ly.C_in, ly.C_out, cfg.T, cfg.decay_len)) return VDT_KERNEL_SORTED;
-    return VDT_KERNEL_CHUNK;
+    return dense_ok ? VDT_KERNEL_DENSE : VDT_KERNEL_CHUNK;
 }
 
 }  // namespace
