@@ -87,9 +87,10 @@ def test_sorted_oversize_chunks_culif(O, dev, C_out):
     assert 0.0 < np.mean(ref < INF) < 1.0
 
 
-@pytest.mark.parametrize("C_out", [256, 512], ids=["team2", "team4"])
+@pytest.mark.parametrize("C_out", [256, 512, 200, 136], ids=["team2", "team4", "team2-partial", "team2-8ch"])
 def test_team_warps_finish_at_different_times(O, dev, C_out):
-    """Each channel group of a pixel gets its own bias (+0.6 down to -0.3):
+    """Each 128-channel group of a pixel gets its own bias (+0.6 down to -0.3;
+    C_out 200 and 136 leave the second group's warp partly or mostly idle):
     every neuron of group 0 fires around step 18, at 512 channels group 1
     around step 43, the last group almost never; inputs spread over every
     chunk.  The warps of a team then run out of live neurons at different
@@ -100,7 +101,7 @@ def test_team_warps_finish_at_different_times(O, dev, C_out):
                        T=80, delta=8, tfs=40.0, lut_mode=nets.LUT_BY_TIN, decay_len=81,
                        readout=nets.READ_ARGMIN_FIRST, tc_in=34.75016403198242, encoder=nets.ENC_LINEAR)
     layers = synth.kaiming_layers(net, 4, gains=[0.4, 1.0])
-    groups = C_out // 128
+    groups = (C_out + 127) // 128                            # the last group may be partly empty
     for g in range(groups):
         layers[0].bias[g * 128:(g + 1) * 128] = 0.6 - 0.9 * g / (groups - 1)
     rng = np.random.default_rng(7)
@@ -109,7 +110,7 @@ def test_team_warps_finish_at_different_times(O, dev, C_out):
     x = x.astype(np.float32)
     ref = O.run_net(net, layers, x, keep=True)
     m0 = ref["maps"][0].reshape(B, H, W, C_out)
-    first = [float(np.mean(m0[..., g * 128:(g + 1) * 128] < INF)) for g in range(groups)]
+    first = [float(np.mean(m0[..., g * 128:min(C_out, (g + 1) * 128)] < INF)) for g in range(groups)]
     assert first[0] > 0.9 and first[-1] < 0.5, f"fired fraction per group {first}"
     done0 = np.mean(m0[..., :128].reshape(-1, 128).max(1) < INF)   # pixels whose group-0 warp finishes early
     assert done0 > 0.9, done0
