@@ -357,9 +357,13 @@ cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t 
     const size_t smem = (size_t)DW * dense_words(ntaps * p.C_in, p.T, ntaps) * sizeof(int) +
                         (size_t)(p.decay_len + 2 * p.T) * sizeof(float);
     // register budget tuned for occupancy (the kernel is latency-bound): the
-    // streamed block, lane state and the sort's input registers
+    // streamed block, lane state and the sort's input registers, at most 8
+    // CTAs per SM; measured exceptions: one 32-input window runs 16 CTAs (32
+    // registers), and 18 windows at 4 channels per lane 9 CTAs (56 registers,
+    // the shared-memory limit at 576 inputs; 2 channels per lane stay at 8)
     constexpr int REGS = FS * V + 2 * FS + (CULIF ? 5 : 4) * V + R;
-    constexpr int MINB = (65536 / (DW * 32 * REGS)) > 8 ? 8 : (65536 / (DW * 32 * REGS));
+    constexpr int MINB0 = (65536 / (DW * 32 * REGS)) > 8 ? 8 : (65536 / (DW * 32 * REGS));
+    constexpr int MINB = CULIF ? MINB0 : (R == 18 && V == 4) ? 9 : (R == 1 ? 16 : MINB0);
     auto kern = CULIF ? k_dense<V, R, MINB, false, true>
                       : (p.fetched ? k_dense<V, R, MINB, true, false> : k_dense<V, R, MINB, false, false>);
     if (smem > 48 * 1024) {
