@@ -40,6 +40,7 @@ constexpr int SWARPS = 4;    // warps per CTA
 constexpr int FS = 8;        // records per streamed block
 constexpr int MAXS = 64;     // slots per chunk (DELTA <= 64)
 constexpr int ROW_MASK = 0xffffff;      // decoded record.x: row | slot << 24
+constexpr int META_NRUNS = SWARPS;      // s_meta: [0, G) alive flags, then the run count
 
 // records per team buffer: 256 for one warp per pixel (so that 8 CTAs fit
 // in shared memory), 512 for teams of 2 or 4 warps
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
     int* s_pre = s_wrow + 32;
     int* s_st = s_pre + 32;
     int2* s_runs = reinterpret_cast<int2*>(s_st + 32);      // [MAXS] chunk runs
-    int* s_meta = s_st + 32 + 2 * MAXS;                      // [G] alive flags, [4] run count
+    int* s_meta = s_st + 32 + 2 * MAXS;                      // [G] alive flags, [META_NRUNS] run count
     int* s_off = s_meta + 8;                                 // [ntaps][OS]
     float* s_decay = reinterpret_cast<float*>(sm + (SWARPS / G) * words);
     float* s_th = s_decay + p.decay_len;
@@ -252,7 +253,7 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
             if (lane == 0) s_start[nb] = prev;
             __syncwarp();
             const int nr = compact_runs(s_start + 1, nb, rbase, s_runs);
-            if (lane == 0) s_meta[4] = nr;
+            if (lane == 0) s_meta[META_NRUNS] = nr;
         }
         team_sync<G>(team);
         for (int w0 = lo; w0 < hi; w0 += 32) {
@@ -276,7 +277,7 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
             __syncwarp();
         }
         team_sync<G>(team);
-        return s_meta[4];
+        return s_meta[META_NRUNS];
     };
 
     for (int tau = 0; tau < p.NC; ++tau) {
