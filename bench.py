@@ -198,13 +198,15 @@ def launches_per_step(net, kernels, pixels=True):
     pixel encoder; per layer its integrator, plus a bucketize pass unless the
     integrator reads the spike map itself (k_dense, k_thread, k_layer_vmem),
     plus a pool pass unless the pool runs fused into the integrator
-    (k_thread); the readout unless the last layer is a membrane readout (it
-    runs fused there).  Each sub-batch launches the same sequence."""
-    from vdttfs.engine import KERNEL_DENSE, KERNEL_THREAD, KERNEL_VMEM
+    (k_thread, k_dense, k_sorted: everything but the generic chunk
+    integrator); the readout unless the last layer is a membrane readout (it
+    runs fused there).  Each sub-batch launches the same sequence.  The fused
+    pools' pre-fill is a memset node, not a kernel."""
+    from vdttfs.engine import KERNEL_CHUNK, KERNEL_DENSE, KERNEL_THREAD, KERNEL_VMEM
     n = 1 if pixels else 0
     for l, k in zip(net.layers, kernels):
         n += 1 if k in (KERNEL_DENSE, KERNEL_THREAD, KERNEL_VMEM) else 2
-        n += 1 if l.pool_after and k != KERNEL_THREAD else 0
+        n += 1 if l.pool_after and k == KERNEL_CHUNK else 0
     return n + (0 if kernels[-1] == KERNEL_VMEM else 1)
 
 

@@ -1,11 +1,12 @@
 """GPU: the work on the edges of the integrators, fused or not, against the oracle.
 
-* A layer's 2x2 min pool (k_pooling, t1:164-181 / t2:192-209): fused into
-  k_thread (which writes the pooled map), a separate pool pass after k_dense
-  and k_sorted (fusing it into those as a CTA per 2x2 quad measured slower).
+* A layer's 2x2 min pool (k_pooling, t1:164-181 / t2:192-209), fused into
+  every integrator that runs the layer: k_thread (a quad of threads) and
+  k_dense / k_sorted (an integer min of each output into its pooled cell).
   The pooled layer is the network's last layer here, so the output compared
   bit for bit IS the pooled map, including odd map sizes (the last row /
-  column dropped) and every channel width the kernels vectorise differently.
+  column dropped) and every channel width the kernels vectorise differently;
+  the traced run writes the unpooled map and pools it in a separate pass.
 * The pixel encoder (k_encode_image's log encoder, t1:32-42 / t2:32-42, and
   the linear one) as a separate pass in front of every first-layer
   integrator (fusing it into the first layer's read measured slower).
@@ -76,7 +77,7 @@ def test_pooled_last_layer_every_integrator(O, dev, case):
     ctx.set_layer_kernel(0, kernel)
     for graphs in (True, False):
         ctx.set_graphs(graphs)
-        out, pred = ctx.infer(_t(spikes))                # not traced: k_thread's pool runs fused
+        out, pred = ctx.infer(_t(spikes))                # not traced: the pool runs fused
         o = _np(out)
         assert o.shape == (B, (H - (0 if pad else k - 1)) // 2 * ((W - (0 if pad else k - 1)) // 2) * co)
         n_bad = int(np.sum(o.view(np.int32) != ref["out"].view(np.int32)))

@@ -264,7 +264,15 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
         for (int dd = 16; dd > 0; dd >>= 1) fetched += __shfl_down_sync(FULL_MASK, fetched, dd);
         if (lane == 0 && fetched) atomicAdd(p.fetched, fetched);
     }
-    if (lane_ok) store_res<V>(p.out + (long long)pix * p.C_out + c0, nu.res);
+    if (lane_ok) {
+        if (p.pool_out) {
+            const unsigned r = pix / (unsigned)p.W_out, q = r / (unsigned)p.H_out;
+            pool_store<V>(p.pool_out, q, (int)(r - q * (unsigned)p.H_out), (int)(pix - r * (unsigned)p.W_out),
+                          p.H_out, p.W_out, p.C_out, c0, nu.res);
+        } else {
+            store_res<V>(p.out + (long long)pix * p.C_out + c0, nu.res);
+        }
+    }
 }
 
 // Two output pixels per warp for layers with at most 16 output channels
@@ -404,7 +412,8 @@ bool dense_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len
 
 cudaError_t launch_dense(const IntegParams& p, const float* in, cudaStream_t s) {
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
-    if (!p.fetched && p.C_out <= 16 && dense_smem(ntaps * p.C_in, p.T, ntaps, p.decay_len, 2) <= 160 * 1024)
+    if (!p.fetched && !p.pool_out && p.C_out <= 16 &&
+        dense_smem(ntaps * p.C_in, p.T, ntaps, p.decay_len, 2) <= 160 * 1024)
         return launch_pair(p, in, s);
     switch (pick_v_dense(p.C_out)) {
         case 4: return launch_dense_v<4, false>(p, in, s);

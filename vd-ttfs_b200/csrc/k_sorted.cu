@@ -387,7 +387,9 @@ __global__ void __launch_bounds__(SWARPS * 32, MINB) k_sorted(IntegParams p, int
         if (!done) nu.close_empty(next_t, p.T, tt);
     }
     if (lane_ok) {
-        if (p.out_nchw) {
+        if (p.pool_out) {
+            pool_store<V>(p.pool_out, img, h_out, w_out, p.H_out, p.W_out, p.C_out, c0, nu.res);
+        } else if (p.out_nchw) {
             const long long plane = (long long)p.H_out * p.W_out;
             const long long site = (long long)h_out * p.W_out + w_out;
 #pragma unroll

@@ -410,6 +410,24 @@ __device__ __forceinline__ void load_row(const float* p, float (&w)[V]) {
     }
 }
 
+// The layer's 2x2 min pool fused into its integrator (k_pool_min's result,
+// t1:164-181 / t2:192-209): output pixel (img, h, w) takes part in pooled
+// cell (h / 2, w / 2) -- none if it lies in the last row or column of an odd
+// map -- by an integer min on the float bits of its V results.  Spike times
+// and the no-spike time are non-negative, so their bits order like their
+// values; the cell starts at the bytes 0x7F (about 3.4e38, above every time)
+// and ends as the minimum of its four outputs, which is what k_pool_min
+// writes (its start value, the no-spike time, is never below them).
+template <int V>
+__device__ __forceinline__ void pool_store(float* pooled, long long img, int h, int w, int H, int W, int C,
+                                           int c0, const float (&r)[V]) {
+    const int Hp = H >> 1, Wp = W >> 1;
+    if ((h >> 1) >= Hp || (w >> 1) >= Wp) return;
+    int* dst = reinterpret_cast<int*>(pooled) + ((img * Hp + (h >> 1)) * Wp + (w >> 1)) * (long long)C + c0;
+#pragma unroll
+    for (int v = 0; v < V; ++v) atomicMin(dst + v, __float_as_int(r[v]));
+}
+
 template <int V>
 __device__ __forceinline__ void store_res(float* p, const float (&r)[V]) {
     if constexpr (V == 1) {

@@ -516,6 +516,20 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
                 StageTimer st(c, i, 0);
                 VDT_CUDA(launch_bucketize(bp, s));
             }
+            // k_dense and k_sorted write the pooled map themselves when nobody
+            // asks for the layer's own map (not traced): an integer min of
+            // each output into its cell, the cells pre-filled with 0x7F bytes
+            // (the times' bits order like their values only when the no-spike
+            // time is positive, as it is in every reference configuration)
+            if (ly.d.pool_after && !(trace && trace[i]) && ly.H_out >= 2 && ly.W_out >= 2 && cfg.inf_time > 0.0f &&
+                (kern == VDT_KERNEL_DENSE || kern == VDT_KERNEL_SORTED)) {
+                float* z = last ? d_out : y;
+                StageTimer sp(c, i, 2);
+                VDT_CUDA(cudaMemsetAsync(z, 0x7F, (size_t)B * (ly.H_out / 2) * (ly.W_out / 2) * ly.C_out * sizeof(float),
+                                         s));
+                ip.pool_out = z;
+                pooled = true;
+            }
             StageTimer st(c, i, 1);
             if (kern == VDT_KERNEL_THREAD && !fe) {
                 // k_thread writes the pooled map itself when nobody asks for

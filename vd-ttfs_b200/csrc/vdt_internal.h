@@ -86,6 +86,10 @@ struct IntegParams {
     float culif_decay, culif_th;
     int out_nchw;
     int in_nchw;   // launch_dense_culif: the input spike map is NCHW [B, C_in, H_in, W_in]
+    // k_dense / k_sorted (LIF conv layers): when set, the layer's 2x2 min pool
+    // [B, H_out / 2, W_out / 2, C_out] is written here instead of the map
+    // (`out` is not written); the caller fills it with the bytes 0x7F first
+    float* pool_out;
 };
 cudaError_t launch_integrate(const IntegParams& p, cudaStream_t s);
 // true when launch_integrate supports this (K, delta, C_out) combination
