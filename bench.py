@@ -39,6 +39,7 @@ configuration it has and its step-by-step (time-driven) programs, and prints
 one line with their throughputs (the reported baselines).
 """
 import argparse
+import gc
 import json
 import os
 import subprocess
@@ -346,16 +347,17 @@ def run_engine(a):
     clocks = ClockSampler(local, enabled=(rank == 0 and not a.no_clocks))
     clocks.start()
     times = []
-    for _ in range(a.steps):
+    evs = timing_events(torch, a.steps)
+    gc.disable()                      # no collector pauses of this harness inside the timed steps
+    for e0, e1 in evs:
         with torch.cuda.stream(stream):
             flush.fill_(1)
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             step()
             e1.record(stream)
         stream.synchronize()
         times.append(e0.elapsed_time(e1))
+    gc.enable()
     clk = clocks.stop()
     tot_ms = float(np.sum(times))
     if world > 1:
@@ -396,17 +398,18 @@ def run_engine(a):
         if world > 1:
             dist.barrier()
         e_times = []
-        for _ in range(a.steps):
+        evs = timing_events(torch, a.steps)
+        gc.disable()
+        for e0, e1 in evs:
             with torch.cuda.stream(stream):
                 flush.fill_(1)
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
             ctx.infer_host(h_in, pixels=True, out=h_out, pred=h_pred)
             with torch.cuda.stream(stream):
                 e1.record(stream)
             stream.synchronize()
             e_times.append(e0.elapsed_time(e1))
+        gc.enable()
         e2e_out, e2e_pred = h_out.numpy(), h_pred.numpy()
     e_ms = float(np.sum(e_times))
     if world > 1:
@@ -517,6 +520,11 @@ def run_engine(a):
 
 
 # --------------------------------------------------------------- CPU legs --
+def timing_events(torch, n):
+    """n (start, stop) CUDA timing event pairs, made before a timed loop."""
+    return [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+
+
 def step_spread(times_ms, steps):
     """min / median / max of the per-step times (one pipelined call over all
     steps gives only its mean)."""
@@ -664,16 +672,18 @@ def run_dvs_engine(a):
     big = frames.nbytes > L2_BYTES
     flush = None if big else torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     times = []
-    for _ in range(a.steps):
+    evs = timing_events(torch, a.steps)
+    gc.disable()
+    for e0, e1 in evs:
         with torch.cuda.stream(stream):
             if flush is not None:
                 flush.fill_(1)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             step()
             e1.record(stream)
         stream.synchronize()
         times.append(e0.elapsed_time(e1))
+    gc.enable()
     clk = clocks.stop()
     tot_ms = float(np.sum(times))
     if world > 1:
@@ -704,16 +714,18 @@ def run_dvs_engine(a):
         e_times = [e0.elapsed_time(e1)]
     else:
         e_times = []
-        for i in range(a.steps):
+        evs = timing_events(torch, a.steps)
+        gc.disable()
+        for i, (e0, e1) in enumerate(evs):
             with torch.cuda.stream(stream):
                 flush.fill_(1)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
             ctx.infer_host(h_in, out=h_outs[i], pred=h_preds[i])
             with torch.cuda.stream(stream):
                 e1.record(stream)
             stream.synchronize()
             e_times.append(e0.elapsed_time(e1))
+        gc.enable()
     e_ms = float(np.sum(e_times))
     if world > 1:
         t = torch.tensor([e_ms], device=dev)
