@@ -196,7 +196,8 @@ def layer_bytes(net, events_per_layer, B):
 
 def launches_per_step(net, kernels, pixels=True):
     """Kernel launches of one inference (graph path, one sub-batch): the
-    pixel encoder; per layer its integrator, plus a bucketize pass unless the
+    pixel encoder unless the first layer runs k_dense (which encodes the
+    pixels as it reads them); per layer its integrator, plus a bucketize pass unless the
     integrator reads the spike map itself (k_dense, k_thread, k_layer_vmem),
     plus a pool pass unless the pool runs fused into the integrator
     (k_thread, k_dense, k_sorted: everything but the generic chunk
@@ -204,7 +205,7 @@ def launches_per_step(net, kernels, pixels=True):
     runs fused there).  Each sub-batch launches the same sequence.  The fused
     pools' pre-fill is a memset node, not a kernel."""
     from vdttfs.engine import KERNEL_CHUNK, KERNEL_DENSE, KERNEL_THREAD, KERNEL_VMEM
-    n = 1 if pixels else 0
+    n = 1 if pixels and kernels[0] != KERNEL_DENSE else 0
     for l, k in zip(net.layers, kernels):
         n += 1 if k in (KERNEL_DENSE, KERNEL_THREAD, KERNEL_VMEM) else 2
         n += 1 if l.pool_after and k == KERNEL_CHUNK else 0

@@ -8,8 +8,10 @@
   column dropped) and every channel width the kernels vectorise differently;
   the traced run writes the unpooled map and pools it in a separate pass.
 * The pixel encoder (k_encode_image's log encoder, t1:32-42 / t2:32-42, and
-  the linear one) as a separate pass in front of every first-layer
-  integrator (fusing it into the first layer's read measured slower).
+  the linear one): fused into k_dense's read of a first layer (the same
+  device function as the separate pass), a separate pass in front of the
+  other first-layer integrators (fusing it into k_thread's read measured
+  slower).
 * The readout (t1:313-315, t2:391-392, t3:295-296) fused into the membrane
   readout layer (k_layer_vmem, t2:172-190), every readout mode.
 Host-libm LUTs, so every comparison is bit for bit.

@@ -62,7 +62,7 @@ size_t dense_smem(int fan, int T, int ntaps, int decay_len, int P) {
 // CULIF: the task-3 rule (tb = (int)t, kept iff 0 <= tb < T, t3:79; the
 // record's LUT value is 1, so the chain adds the weight exactly) and the
 // input map may be NCHW (p.in_nchw).
-template <int R, bool CULIF>
+template <int R, bool CULIF, bool ENC = false>
 __device__ __forceinline__ int sort_pixel(const IntegParams& p, const float* __restrict__ in, unsigned pix,
                                           int fan, int ntaps, int* wb, const float* s_decay) {
     const int lane = threadIdx.x & 31;
@@ -109,7 +109,12 @@ __device__ __forceinline__ int sort_pixel(const IntegParams& p, const float* __r
         if (f < fan) {
             const int j = tap_of(f, p.C_in, inv);
             const long long cb = s_col[j];
-            if (cb >= 0) tv[r] = __ldg(in + cb + (f - j * p.C_in) * cs);
+            if (cb >= 0) {
+                const float v = __ldg(in + cb + (f - j * p.C_in) * cs);
+                // ENC: a first layer reading pixels encodes each one as it is read
+                if constexpr (ENC) tv[r] = encode_pixel(v, p.encoder, p.enc_tc, p.enc_td, p.T, p.inf_time);
+                else tv[r] = v;
+            }
         }
     }
     // input value -> key = tb | LUT index << 16 (bucketize rule), -1 if no event
@@ -181,10 +186,11 @@ __device__ __forceinline__ int sort_pixel(const IntegParams& p, const float* __r
 // CULIF: the task-3 conv_bucketed_early neuron (t3:109-143) fed straight
 // from the spike map: CulifLanes, every step scanned up to NC * delta (the
 // reference scans whole chunks), output NHWC or NCHW (p.out_nchw).
-template <int V, int R, int MINB, bool COUNT, bool CULIF>
+template <int V, int R, int MINB, bool COUNT, bool CULIF, bool ENC = false>
 __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const float* __restrict__ in,
                                                          int n_warps, int groups) {
     static_assert(!(COUNT && CULIF), "no counters on CuLIF layers");
+    static_assert(!(ENC && (COUNT || CULIF)), "the fused encoder is for a LIF first layer outside counting passes");
     extern __shared__ __align__(16) int sm[];
     __shared__ int s_floor, s_mono;
     chain_release();
@@ -213,7 +219,7 @@ __global__ void __launch_bounds__(DW * 32, MINB) k_dense(IntegParams p, const fl
     const int grp = gw - (int)pix * groups;
     const int c0 = (grp * 32 + lane) * V;
     const bool lane_ok = c0 < p.C_out;
-    const int nruns = sort_pixel<R, CULIF>(p, in, pix, fan, ntaps, wb, s_decay);
+    const int nruns = sort_pixel<R, CULIF, ENC>(p, in, pix, fan, ntaps, wb, s_decay);
 
     // 3. stream the runs
     std::conditional_t<CULIF, CulifLanes<V>, Lanes<V>> nu;
@@ -373,7 +379,8 @@ cudaError_t launch_dense_vr(const IntegParams& p, const float* in, cudaStream_t 
     constexpr int MINB0 = (65536 / (DW * 32 * REGS)) > 8 ? 8 : (65536 / (DW * 32 * REGS));
     constexpr int MINB = CULIF ? MINB0 : (R == 18 && V == 4) ? 9 : (R == 1 ? 16 : MINB0);
     auto kern = CULIF ? k_dense<V, R, MINB, false, true>
-                      : (p.fetched ? k_dense<V, R, MINB, true, false> : k_dense<V, R, MINB, false, false>);
+                      : (p.fetched ? k_dense<V, R, MINB, true, false>
+                                   : (p.encoder ? k_dense<V, R, MINB, false, false, true> : k_dense<V, R, MINB, false, false>));
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
@@ -412,7 +419,7 @@ bool dense_supported(int K, int is_fc, int C_in, int C_out, int T, int decay_len
 
 cudaError_t launch_dense(const IntegParams& p, const float* in, cudaStream_t s) {
     const int ntaps = p.is_fc ? 1 : p.K * p.K;
-    if (!p.fetched && !p.pool_out && p.C_out <= 16 &&
+    if (!p.fetched && !p.pool_out && !p.encoder && p.C_out <= 16 &&
         dense_smem(ntaps * p.C_in, p.T, ntaps, p.decay_len, 2) <= 160 * 1024)
         return launch_pair(p, in, s);
     switch (pick_v_dense(p.C_out)) {

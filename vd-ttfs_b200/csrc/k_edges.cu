@@ -45,26 +45,7 @@ __global__ void k_encode(const float* __restrict__ px, float* __restrict__ out, 
     chain_wait();
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
-        const float x = __ldg(px + i);
-        float r;
-        if (encoder == VDT_ENC_LOG) {
-            if (x < 1e-5) {
-                r = inf_time;
-            } else {
-                float tf = fmaf(-tc, logf(x), td);
-                if (tf < 0.0f) tf = 0.0f;
-                const float ts = ceilf(tf);
-                r = ts > (float)T ? inf_time : ts;
-            }
-        } else {
-            if (x < 1e-5f) {
-                r = inf_time;
-            } else {
-                const float ts = floorf(__fmul_rn(__fsub_rn(1.0f, x), (float)T));
-                r = ts > (float)T ? inf_time : ts;
-            }
-        }
-        out[i] = r;
+        out[i] = encode_pixel(__ldg(px + i), encoder, tc, td, T, inf_time);
     }
 }
 

@@ -443,10 +443,12 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
     cudaStream_t s = c->stream;
     const float* x = d_input;
     int ai = 0;
-    // pixels: one encode pass writes the spike times first (fusing it into
-    // the first layer's read measured slower: every output pixel re-encodes
-    // each input of its window)
-    if (pixels && m->net.encoder != VDT_ENC_NONE) {
+    // pixels: a first layer on k_dense encodes them as it reads its windows
+    // (unless counting, whose bucket pass needs the spike times); otherwise
+    // one encode pass writes the spike times first
+    const bool encode_fused = pixels && m->net.encoder != VDT_ENC_NONE && !c->counting &&
+                              layer_kernel(c, 0, cfg) == VDT_KERNEL_DENSE;
+    if (pixels && m->net.encoder != VDT_ENC_NONE && !encode_fused) {
         const long long n = (long long)B * m->net.in_h * m->net.in_w * m->net.in_c;
         VDT_CUDA(launch_encode(d_input, c->act[0], n, m->net.encoder, m->net.tc_in, m->net.td_in,
                                cfg.T, cfg.inf_time, s));
@@ -495,6 +497,9 @@ int enqueue(vdt_ctx* c, const float* d_input, int pixels, int B, float* d_out, i
             ip.lut_mode = cfg.lut_mode; ip.decay_len = cfg.decay_len;
             ip.tfs = cfg.fire_start; ip.inf_time = cfg.inf_time;
             ip.fetched = fe;
+            if (i == 0 && encode_fused) {
+                ip.encoder = m->net.encoder; ip.enc_tc = m->net.tc_in; ip.enc_td = m->net.td_in;
+            }
             const bool dense = kern == VDT_KERNEL_DENSE || kern == VDT_KERNEL_THREAD;
             if (!dense || ev) {
                 // the dense path needs no buckets; they are still built when

@@ -90,7 +90,27 @@ struct IntegParams {
     // [B, H_out / 2, W_out / 2, C_out] is written here instead of the map
     // (`out` is not written); the caller fills it with the bytes 0x7F first
     float* pool_out;
+    // k_dense (LIF): the input map holds pixels, encoded with encode_pixel
+    // as they are read (VDT_ENC_NONE: spike times)
+    int encoder;
+    float enc_tc, enc_td;
 };
+
+// k_encode_image's log encoder (t1:32-42, t2:32-42) and the linear
+// t = floor((1 - x) * T) encoder for one pixel value; shared by k_encode and
+// the first layer's fused read, so both give the same bits
+__device__ __forceinline__ float encode_pixel(float x, int encoder, float tc, float td, int T, float inf_time) {
+    if (encoder == VDT_ENC_LOG) {
+        if (x < 1e-5) return inf_time;
+        float tf = fmaf(-tc, logf(x), td);
+        if (tf < 0.0f) tf = 0.0f;
+        const float ts = ceilf(tf);
+        return ts > (float)T ? inf_time : ts;
+    }
+    if (x < 1e-5f) return inf_time;
+    const float ts = floorf(__fmul_rn(__fsub_rn(1.0f, x), (float)T));
+    return ts > (float)T ? inf_time : ts;
+}
 cudaError_t launch_integrate(const IntegParams& p, cudaStream_t s);
 // true when launch_integrate supports this (K, delta, C_out) combination
 bool integrate_supported(int K, int is_fc, int delta, int C_out, int T, int decay_len);
