@@ -175,3 +175,34 @@ def test_unpooled_conv_last_layer_output_is_the_whole_map(O, dev):
         assert bits_equal(o2, ref["out"]) and np.array_equal(p2, ref["pred"])
     ctx.close()
     m.close()
+
+
+@pytest.mark.parametrize("kernel", [DENSE, SORTED, CHUNK])
+def test_pooled_middle_layer_feeds_the_next(O, dev, kernel):
+    """A pooled layer inside the network (odd 7x9 map: the last row and
+    column dropped) on each integrator: the next layer reads the pooled map
+    the integrator wrote (k_dense / k_sorted fused, the chunk integrator with
+    a pool pass), graph and eager paths, with sub-batches, bit for bit."""
+    from vdttfs import engine as E, nets, synth
+    net = nets.NetSpec("midpool", 7, 9, 16, (nets._conv(16, 64, 3, nets.PAD_SAME, True), nets._conv(64, 32, 3, nets.PAD_SAME),
+                                             nets._fc(3 * 4 * 32, 10)),
+                       T=40, delta=4, tfs=40.0, lut_mode=nets.LUT_BY_TIN, decay_len=41,
+                       readout=nets.READ_ARGMIN_FIRST, tc_in=34.75016403198242, encoder=nets.ENC_LINEAR)
+    layers = synth.kaiming_layers(net, 5, gains=[1.4, 1.3, 1.0])
+    B = 9
+    spikes = O.encode_linear(synth.images(5, B, 7, 9, 16, 0.3, stream=39), net.T)
+    ref = O.run_net(net, layers, spikes, keep=True)
+    assert 0.05 < np.mean(ref["maps"][1] < net.inf_time) < 0.95     # the pooled map
+    assert 0.0 < np.mean(ref["maps"][2] < net.inf_time)             # the next layer fires
+    m = E.Model(net, layers, lut_source=E.LUT_HOST_LIBM)
+    ctx = E.Context(m, B)
+    ctx.set_layer_kernel(0, kernel)
+    for sub in (1, 2):
+        ctx.set_sub_batches(sub)
+        for graphs in (True, False):
+            ctx.set_graphs(graphs)
+            out, pred = ctx.infer(_t(spikes))
+            assert bits_equal(_np(out), ref["out"]), f"sub={sub} graphs={graphs}"
+            assert np.array_equal(_np(pred), ref["pred"])
+    ctx.close()
+    m.close()
